@@ -1,0 +1,336 @@
+"""Benchmark of the quantized decode GEMV path (BASELINE.json metric: weight-stream
+GB/s per quant matvec).
+
+Workload (the configuration the metric is quoted on): one step =
+one batch-1 GEMV over each of 16 resident packs, {Q4_K, Q5_K, IQ2_S, IQ3_S} x
+{4096x4096, 14336x4096, 4096x14336, 128256x8192} (out x in), through the C-ABI
+entry point qg_gemv.  Packs are seeded synthetic data with the BASELINE
+distributions; 2.37 GB of packs per step, far larger than L2, so no flush is needed.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+value       = algorithmic bytes (packed weights + x + y) of all GEMVs / device time,
+              summed over ranks (each rank runs the whole sweep: weak scaling).
+e2e         = the same metric with every step's x copied from pinned host memory and
+              every y copied back inside the timed region.
+roofline    = the dominant GEMV's algorithmic bytes / its CUDA-event time vs the
+              measured HBM copy bandwidth (MEASURED_PEAKS.json).
+cpu_baseline= the reference's own CPU matvec (oracle/_ref; the C restatement if the
+              reference was not built) on a bounded row sample, all host threads.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO / "local-ai-gpu-acceleration_b200"))
+
+import numpy as np  # noqa: E402
+
+from qgemv_b200 import packs  # noqa: E402
+
+SWEEP_FORMATS = [packs.Q4K_RAW, packs.Q5K, packs.IQ2S, packs.IQ3S]
+SWEEP_SHAPES = [(4096, 4096), (14336, 4096), (4096, 14336), (128256, 8192)]
+FALLBACK_HBM_GBS = 6650.0
+METRIC = "weight-stream GB/s, quant matvec sweep (Q4_K/Q5_K/IQ2_S/IQ3_S x 4 shapes, batch 1)"
+CONFIG = {
+    "workload": "BASELINE config 2: batch-1 GEMV sweep {Q4_K,Q5_K,IQ2_S,IQ3_S} x "
+                "{4096x4096,14336x4096,4096x14336,128256x8192} (out x in), 16 GEMVs per step",
+    "batch": 1,
+    "l2": "no flush: 2.37 GB of packs streamed per step (> 126 MB L2)",
+    "entry_point": "qg_gemv (C-ABI)",
+}
+
+
+def algorithmic_bytes(fmt: int, rows: int, cols: int, batch: int = 1) -> int:
+    return packs.pack_bytes(fmt, rows, cols) + 4 * batch * (cols + rows)
+
+
+def measured_peak() -> tuple[float, str]:
+    path = REPO / "MEASURED_PEAKS.json"
+    if path.exists():
+        try:
+            return float(json.loads(path.read_text())["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs)"
+        except Exception:
+            pass
+    return FALLBACK_HBM_GBS, "fallback 6.65 TB/s"
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks / throttle reasons during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.out = ""
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                self.out, _ = self.proc.communicate()
+
+    def summary(self) -> dict:
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in (self.out or "").splitlines():
+            f = [p.strip() for p in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax.append(float(f[2]))
+            except ValueError:
+                continue
+            for name, val in zip(names, f[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax),
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def cpu_reference_sample(row_fraction: int, threads: int, seed: int = 0) -> dict:
+    """Time the reference's CPU matvec on the first rows/row_fraction rows of every
+    sweep matrix (same formats, cols and value distributions)."""
+    sys.path.insert(0, str(REPO / "oracle"))
+    import qoracle
+
+    ref = qoracle.Ref.load(build=False)
+    kind = "reference"
+    if ref is None:
+        ref, kind = None, "port"
+        port = qoracle.Port()
+    total_bytes, total_t = 0, 0.0
+    for fmt in SWEEP_FORMATS:
+        for rows, cols in SWEEP_SHAPES:
+            r = max(16, rows // row_fraction)
+            pk = packs.synthetic_pack(fmt, r, cols, seed=seed + fmt * 7 + rows + cols)
+            x = packs.synthetic_activation(cols, fmt)
+            if ref is not None:
+                t, _ = ref.time_matvec(fmt, pk.payload, pk.meta, x, r, cols, threads)
+            else:
+                t0 = time.perf_counter()
+                port.matvec(fmt, pk.payload, pk.meta, x, r, cols)
+                t = time.perf_counter() - t0
+            total_t += t
+            total_bytes += algorithmic_bytes(fmt, r, cols)
+    used = threads if kind == "reference" else 1
+    return {"value": total_bytes / total_t / 1e9, "unit": "GB/s", "cores": used, "kind": kind,
+            "sample": f"first rows/{row_fraction} rows (min 16) of each of the 16 sweep matrices, "
+                      f"{total_bytes / 1e6:.1f} MB of packs, {total_t:.2f} s wall on {used} threads"}
+
+
+def run_reference(args) -> int:
+    if int(os.environ.get("RANK", "0")) != 0:
+        return 0
+    threads = os.cpu_count() or 1
+    fraction = 32
+    cpu_reference_sample(256, threads)  # warm-up of the code path (not timed)
+    vals = []
+    for _ in range(args.warmup):
+        cpu_reference_sample(fraction, threads, seed=1)
+    t0 = time.perf_counter()
+    for k in range(args.steps):
+        vals.append(cpu_reference_sample(fraction, threads, seed=2 + k))
+    elapsed = time.perf_counter() - t0
+    value = statistics.median(v["value"] for v in vals)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "GB/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": elapsed / max(1, args.steps) * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded packs, BASELINE distributions)",
+        "config": dict(CONFIG, sample=vals[0]["sample"]),
+        "cpu_baseline": {k: vals[0][k] for k in ("kind", "cores", "sample")} | {"value": value, "unit": "GB/s"},
+        "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line))
+    return 0
+
+
+def run_ours(args) -> int:
+    import torch
+    import torch.distributed as dist
+
+    from qgemv_b200 import check, ops
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+
+    # Resident packs + activations (setup, untimed).
+    mats = []
+    xs = {}
+    for fmt in SWEEP_FORMATS:
+        for rows, cols in SWEEP_SHAPES:
+            pk = packs.synthetic_pack(fmt, rows, cols, seed=1000 * fmt + rows + cols)
+            payload, meta = ops.to_device(pk, device)
+            if cols not in xs:
+                xs[cols] = torch.from_numpy(packs.synthetic_activation(cols, cols)).to(device)
+            y = torch.empty(rows, dtype=torch.float32, device=device)
+            mats.append({"fmt": fmt, "rows": rows, "cols": cols, "payload": payload, "meta": meta,
+                         "y": y, "bytes": algorithmic_bytes(fmt, rows, cols)})
+            del pk
+    stream = torch.cuda.current_stream(device)
+    sh = stream.cuda_stream
+
+    def launch(m, x):
+        check("qg_gemv", m["fmt"], m["payload"].data_ptr(),
+              None if m["meta"] is None else m["meta"].data_ptr(), x.data_ptr(),
+              m["y"].data_ptr(), m["rows"], m["cols"], sh)
+
+    def step(events=None):
+        for i, m in enumerate(mats):
+            launch(m, xs[m["cols"]])
+            if events is not None:
+                events[i + 1].record(stream)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+
+    # Timed region: K steps, an event after every GEMV (per-kernel durations).
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(len(mats) + 1)] for _ in range(args.steps)]
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        time.sleep(0.4)
+        t_begin = torch.cuda.Event(enable_timing=True)
+        t_end = torch.cuda.Event(enable_timing=True)
+        t_begin.record(stream)
+        for k in range(args.steps):
+            evs[k][0].record(stream)
+            step(evs[k])
+        t_end.record(stream)
+        torch.cuda.synchronize()
+    elapsed_ms = t_begin.elapsed_time(t_end)
+    if world > 1:
+        t = torch.tensor([elapsed_ms], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed_ms = float(t.item())
+        dist.barrier()
+    bytes_per_step = sum(m["bytes"] for m in mats)
+    value = world * bytes_per_step * args.steps / (elapsed_ms * 1e-3) / 1e9
+
+    per = []
+    for i, m in enumerate(mats):
+        ms = statistics.mean(evs[k][i].elapsed_time(evs[k][i + 1]) for k in range(args.steps))
+        per.append({"format": packs.FORMAT_NAMES[m["fmt"]], "rows": m["rows"], "cols": m["cols"],
+                    "ms": ms, "GBps": m["bytes"] / (ms * 1e-3) / 1e9})
+    peak, peak_src = measured_peak()
+    dom = max(range(len(mats)), key=lambda i: per[i]["ms"])
+    dm = mats[dom]
+    roofline = {
+        "bound": "hbm", "kernel": f"gemv_kernel<{packs.FORMAT_NAMES[dm['fmt']]}> {dm['rows']}x{dm['cols']}",
+        "achieved": per[dom]["GBps"], "peak": peak, "unit": "GB/s",
+        "frac": per[dom]["GBps"] / peak, "peak_source": peak_src,
+        "algorithmic_bytes_per_launch": dm["bytes"], "traffic": None,
+    }
+    for row in per:
+        row["frac_of_peak"] = row["GBps"] / peak
+
+    # End to end through the C-ABI: x from pinned host memory, y back, every step.
+    host_x = {c: xs[c].cpu().pin_memory() for c in xs}
+    host_y = [torch.empty(m["rows"], dtype=torch.float32).pin_memory() for m in mats]
+    dev_x = [torch.empty(m["cols"], dtype=torch.float32, device=device) for m in mats]
+    h2d = sum(4 * m["cols"] for m in mats)
+    d2h = sum(4 * m["rows"] for m in mats)
+
+    def e2e_step():
+        for i, m in enumerate(mats):
+            dev_x[i].copy_(host_x[m["cols"]], non_blocking=True)
+            launch(m, dev_x[i])
+            host_y[i].copy_(m["y"], non_blocking=True)
+
+    for _ in range(max(3, args.warmup)):
+        e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([e2e_ms], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_value = world * bytes_per_step * args.steps / (e2e_ms * 1e-3) / 1e9
+
+    err = ops.get_error()
+    if rank == 0:
+        cpu = cpu_reference_sample(8, os.cpu_count() or 1) if world == 1 else None
+        line = {
+            "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded packs, BASELINE distributions)",
+            "config": CONFIG,
+            "roofline": roofline,
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
+            "gpu_launches": len(mats) * args.steps,
+            "clocks": clocks.summary(),
+            "error_word": err,
+            "per_matvec": per,
+        }
+        print(json.dumps(line))
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

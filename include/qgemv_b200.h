@@ -1,0 +1,262 @@
+/*
+ * qgemv_b200.h -- C-ABI of the B200 (sm_100a) quantized decode GEMV library
+ * (libqgemv_b200.so).
+ *
+ * Two groups of entry points:
+ *
+ *  1. Drop-in launchers.  Same names, argument lists, argument meaning and error
+ *     behaviour as the reference's `extern "C"` launchers in
+ *     runtime/kernels/decode/decode_kernels.h (cited per declaration).  An app of
+ *     the reference links this library instead of decode_kernels.cu and runs
+ *     unchanged: logits for the launched rows, the KV page write with the
+ *     pre-update token, then token = (argmax + token + 1) % 32000.
+ *
+ *  2. New entry points (prefix qg_): pure GEMV over any of the eight pack formats,
+ *     batch > 1, the fused layer-slice epilogues, dequantize-to-fp32, and the
+ *     error word.  They have no counterpart in the reference unless a citation
+ *     says so.
+ *
+ * Every pointer is caller-owned device memory unless stated otherwise.  No entry
+ * point allocates, synchronizes or touches host memory (qg_get_error excepted), so
+ * all of them can be recorded into a CUDA graph.  Errors: invalid arguments return
+ * cudaErrorInvalidValue before any launch; otherwise the result of
+ * cudaGetLastError() after the launches.
+ */
+#ifndef QGEMV_B200_H_
+#define QGEMV_B200_H_
+
+#include <cuda_runtime_api.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---------------------------------------------------------------------------
+ * Pack formats.  Byte layouts are the reference's resident packs:
+ *   Q4K_RAW            144 B GGUF blocks {f16 d, f16 dmin, u8 scales[12], u8 qs[128]}
+ *                      (decode_kernels.cu:1920-2001)
+ *   Q4K_SPLIT_*        payload stream 128 B/blk (= block[16:144]) plus a metadata
+ *                      stream (tools/bench/q4k_resident_pack.py:82-145):
+ *     PREDECODED       64 B/blk: 8 x {f32 d*scale, f32 dmin*min}
+ *     HALF             32 B/blk: 8 x {f16 d*scale, f16 dmin*min}
+ *     COMPACT          20 B/blk: {f16 d, f16 dmin, u8 scale[8], u8 min[8]}
+ *     NATIVE           16 B/blk: block[0:16]
+ *   Q5K                176 B {f16 d, f16 dmin, scales[12], qh[32], qs[128]}
+ *   IQ2S               82 B  {f16 d, qs[64], qh[8], scales[8]}
+ *   IQ3S               110 B {f16 d, qs[64], qh[8], signs[32], scales[4]}
+ * Each block holds 256 consecutive values of one row; a row of `cols` values is
+ * cols/256 consecutive blocks; rows are stored one after another.
+ * ------------------------------------------------------------------------- */
+typedef enum qg_format {
+  QG_FMT_Q4K_RAW = 0,
+  QG_FMT_Q4K_SPLIT_PREDECODED = 1,
+  QG_FMT_Q4K_SPLIT_HALF = 2,
+  QG_FMT_Q4K_SPLIT_COMPACT = 3,
+  QG_FMT_Q4K_SPLIT_NATIVE = 4,
+  QG_FMT_Q5K = 5,
+  QG_FMT_IQ2S = 6,
+  QG_FMT_IQ3S = 7,
+  QG_FMT_COUNT = 8
+} qg_format;
+
+/* Bytes per 256-value block in the payload stream. */
+static inline uint32_t qg_payload_bytes_per_block(int fmt) {
+  switch (fmt) {
+    case QG_FMT_Q4K_RAW: return 144u;
+    case QG_FMT_Q4K_SPLIT_PREDECODED:
+    case QG_FMT_Q4K_SPLIT_HALF:
+    case QG_FMT_Q4K_SPLIT_COMPACT:
+    case QG_FMT_Q4K_SPLIT_NATIVE: return 128u;
+    case QG_FMT_Q5K: return 176u;
+    case QG_FMT_IQ2S: return 82u;
+    case QG_FMT_IQ3S: return 110u;
+    default: return 0u;
+  }
+}
+
+/* Bytes per 256-value block in the metadata stream (0 = no metadata stream). */
+static inline uint32_t qg_meta_bytes_per_block(int fmt) {
+  switch (fmt) {
+    case QG_FMT_Q4K_SPLIT_PREDECODED: return 64u;
+    case QG_FMT_Q4K_SPLIT_HALF: return 32u;
+    case QG_FMT_Q4K_SPLIT_COMPACT: return 20u;
+    case QG_FMT_Q4K_SPLIT_NATIVE: return 16u;
+    default: return 0u;
+  }
+}
+
+/* Error word bits (set by kernels, read and cleared by qg_get_error). */
+#define QG_ERR_WAIT_TIMEOUT 0x1u /* a bounded wait on a TMA barrier ran out */
+
+/* ===========================================================================
+ * 1. Drop-in launchers (reference: runtime/kernels/decode/decode_kernels.h)
+ * ========================================================================= */
+
+/* decode_kernels.h:424-435 (raw 144-B Q4_K blocks; all rows). */
+cudaError_t rtxllm_launch_q4k_matvec_decode(
+    const uint8_t* q4k_blocks, const float* activation, float* logits, float* kv,
+    uint32_t* token, uint32_t rows, uint32_t cols, uint32_t kv_words, uint32_t page_words,
+    uint32_t active_pages, cudaStream_t stream);
+/* decode_kernels.h:437-448 */
+cudaError_t rtxllm_launch_q4k_matvec_decode_shared(
+    const uint8_t* q4k_blocks, const float* activation, float* logits, float* kv,
+    uint32_t* token, uint32_t rows, uint32_t cols, uint32_t kv_words, uint32_t page_words,
+    uint32_t active_pages, cudaStream_t stream);
+/* decode_kernels.h:450-461 */
+cudaError_t rtxllm_launch_q4k_matvec_decode_warp(
+    const uint8_t* q4k_blocks, const float* activation, float* logits, float* kv,
+    uint32_t* token, uint32_t rows, uint32_t cols, uint32_t kv_words, uint32_t page_words,
+    uint32_t active_pages, cudaStream_t stream);
+/* decode_kernels.h:463-474 */
+cudaError_t rtxllm_launch_q4k_matvec_decode_warp_broadcast(
+    const uint8_t* q4k_blocks, const float* activation, float* logits, float* kv,
+    uint32_t* token, uint32_t rows, uint32_t cols, uint32_t kv_words, uint32_t page_words,
+    uint32_t active_pages, cudaStream_t stream);
+/* decode_kernels.h:476-487 */
+cudaError_t rtxllm_launch_q4k_matvec_decode_warp_broadcast_vec4(
+    const uint8_t* q4k_blocks, const float* activation, float* logits, float* kv,
+    uint32_t* token, uint32_t rows, uint32_t cols, uint32_t kv_words, uint32_t page_words,
+    uint32_t active_pages, cudaStream_t stream);
+/* decode_kernels.h:489-500 */
+cudaError_t rtxllm_launch_q4k_matvec_decode_warp_broadcast_vec4x2(
+    const uint8_t* q4k_blocks, const float* activation, float* logits, float* kv,
+    uint32_t* token, uint32_t rows, uint32_t cols, uint32_t kv_words, uint32_t page_words,
+    uint32_t active_pages, cudaStream_t stream);
+/* decode_kernels.h:502-513 */
+cudaError_t rtxllm_launch_q4k_matvec_decode_warp_broadcast_vec4x4(
+    const uint8_t* q4k_blocks, const float* activation, float* logits, float* kv,
+    uint32_t* token, uint32_t rows, uint32_t cols, uint32_t kv_words, uint32_t page_words,
+    uint32_t active_pages, cudaStream_t stream);
+/* decode_kernels.h:515-527.  The (scale*d, min*dmin) side table is accepted for
+ * signature compatibility; the raw blocks already carry the same information. */
+cudaError_t rtxllm_launch_q4k_matvec_decode_predecoded_vec4x4(
+    const uint8_t* q4k_blocks, const float* q4k_scale_min_pairs, const float* activation,
+    float* logits, float* kv, uint32_t* token, uint32_t rows, uint32_t cols,
+    uint32_t kv_words, uint32_t page_words, uint32_t active_pages, cudaStream_t stream);
+/* decode_kernels.h:529-541 */
+cudaError_t rtxllm_launch_q4k_matvec_decode_split_predecoded_vec4x4(
+    const uint8_t* q4k_payload, const float* q4k_scale_min_pairs, const float* activation,
+    float* logits, float* kv, uint32_t* token, uint32_t rows, uint32_t cols,
+    uint32_t kv_words, uint32_t page_words, uint32_t active_pages, cudaStream_t stream);
+/* decode_kernels.h:543-555 */
+cudaError_t rtxllm_launch_q4k_matvec_decode_split_half_vec4x4(
+    const uint8_t* q4k_payload, const uint16_t* q4k_scale_min_half_pairs,
+    const float* activation, float* logits, float* kv, uint32_t* token, uint32_t rows,
+    uint32_t cols, uint32_t kv_words, uint32_t page_words, uint32_t active_pages,
+    cudaStream_t stream);
+/* decode_kernels.h:557-569 */
+cudaError_t rtxllm_launch_q4k_matvec_decode_split_compact_vec4x4(
+    const uint8_t* q4k_payload, const uint8_t* q4k_compact_meta, const float* activation,
+    float* logits, float* kv, uint32_t* token, uint32_t rows, uint32_t cols,
+    uint32_t kv_words, uint32_t page_words, uint32_t active_pages, cudaStream_t stream);
+/* decode_kernels.h:571-583 */
+cudaError_t rtxllm_launch_q4k_matvec_decode_split_native_vec4x4(
+    const uint8_t* q4k_payload, const uint8_t* q4k_native_meta, const float* activation,
+    float* logits, float* kv, uint32_t* token, uint32_t rows, uint32_t cols,
+    uint32_t kv_words, uint32_t page_words, uint32_t active_pages, cudaStream_t stream);
+
+/* decode_kernels.h:345-357.  Rows [0, min(rows, rows_limit)) only. */
+cudaError_t rtxllm_launch_q5k_matvec_decode_probe(
+    const uint8_t* q5k_blocks, const float* activation, float* logits, float* kv,
+    uint32_t* token, uint32_t rows, uint32_t cols, uint32_t rows_limit, uint32_t kv_words,
+    uint32_t page_words, uint32_t active_pages, cudaStream_t stream);
+/* decode_kernels.h:359-366 (logits only: no KV write, no token update). */
+cudaError_t rtxllm_launch_iq2s_matvec_probe(
+    const uint8_t* iq2s_blocks, const float* activation, float* logits, uint32_t rows,
+    uint32_t cols, uint32_t rows_limit, cudaStream_t stream);
+/* decode_kernels.h:368-380 */
+cudaError_t rtxllm_launch_iq2s_matvec_decode_probe(
+    const uint8_t* iq2s_blocks, const float* activation, float* logits, float* kv,
+    uint32_t* token, uint32_t rows, uint32_t cols, uint32_t rows_limit, uint32_t kv_words,
+    uint32_t page_words, uint32_t active_pages, cudaStream_t stream);
+/* decode_kernels.h:382-394 */
+cudaError_t rtxllm_launch_iq3s_matvec_decode_probe(
+    const uint8_t* iq3s_blocks, const float* activation, float* logits, float* kv,
+    uint32_t* token, uint32_t rows, uint32_t cols, uint32_t rows_limit, uint32_t kv_words,
+    uint32_t page_words, uint32_t active_pages, cudaStream_t stream);
+
+/* decode_kernels.h:319-325: token = (argmax(logits[0:rows]) + token_offset) % vocab_size. */
+cudaError_t rtxllm_launch_output_token_sample(
+    const float* logits, uint32_t* token, uint32_t rows, uint32_t vocab_size,
+    uint32_t token_offset, cudaStream_t stream);
+
+/* Feedback kernels of the mixed layer-slice runner (decode_kernels.h:38-101).  All use
+ * the unweighted RMS of logits[0:rows] and index logits[col % rows]. */
+cudaError_t rtxllm_launch_rmsnorm_feedback(
+    const float* logits, float* activation, uint32_t rows, uint32_t cols, float epsilon,
+    cudaStream_t stream);
+cudaError_t rtxllm_launch_silu_rmsnorm_feedback(
+    const float* logits, float* activation, uint32_t rows, uint32_t cols, float epsilon,
+    cudaStream_t stream);
+cudaError_t rtxllm_launch_rmsnorm_feedback_with_silu_cache(
+    const float* logits, float* activation, float* silu_cache, uint32_t rows, uint32_t cols,
+    float epsilon, cudaStream_t stream);
+cudaError_t rtxllm_launch_gated_silu_rmsnorm_feedback(
+    const float* logits, const float* silu_cache, float* activation, uint32_t rows,
+    uint32_t cache_cols, uint32_t cols, float epsilon, cudaStream_t stream);
+cudaError_t rtxllm_launch_rmsnorm_silu_cache(
+    const float* logits, float* silu_cache, uint32_t rows, uint32_t cache_cols, float epsilon,
+    uint32_t accumulate, cudaStream_t stream);
+cudaError_t rtxllm_launch_rmsnorm_cache(
+    const float* logits, float* cache, uint32_t rows, uint32_t cache_cols, float epsilon,
+    uint32_t accumulate, cudaStream_t stream);
+cudaError_t rtxllm_launch_rmsnorm_cache_and_gated_product(
+    const float* logits, const float* gate_cache, float* up_cache, float* activation,
+    uint32_t rows, uint32_t cache_cols, uint32_t output_cols, float epsilon,
+    uint32_t accumulate, cudaStream_t stream);
+
+/* ===========================================================================
+ * 2. New entry points
+ * ========================================================================= */
+
+/* y[r] = sum_c W[r, c] * x[c] for r < rows.  `meta` is the metadata stream for the
+ * Q4K_SPLIT_* formats and ignored otherwise.  cols must be a positive multiple of
+ * 256.  No KV write, no token update. */
+cudaError_t qg_gemv(int fmt, const uint8_t* payload, const uint8_t* meta, const float* x,
+                    float* y, uint32_t rows, uint32_t cols, cudaStream_t stream);
+
+/* One decode stage with the reference launchers' semantics (decode_kernels.cu:
+ * 4032-4177): y for rows [0, rows), KV page write with the pre-update token for
+ * rows < active_pages (kv may be NULL), then
+ * token = (argmax(y[0:rows]) + token + 1) % 32000. */
+cudaError_t qg_decode_stage(int fmt, const uint8_t* payload, const uint8_t* meta,
+                            const float* x, float* y, float* kv, uint32_t* token,
+                            uint32_t rows, uint32_t cols, uint32_t kv_words,
+                            uint32_t page_words, uint32_t active_pages, cudaStream_t stream);
+
+/* Y[b, r] = sum_c W[r, c] * X[b, c] for b < batch (X row-major [batch, cols] fp32,
+ * Y row-major [batch, rows]).  batch 1..32. */
+cudaError_t qg_gemv_batched(int fmt, const uint8_t* payload, const uint8_t* meta,
+                            const float* x, float* y, uint32_t batch, uint32_t rows,
+                            uint32_t cols, cudaStream_t stream);
+
+/* Dequantize blocks [first_block, first_block + block_count) of a pack into
+ * out[block_count * 256] (fp32, bit-identical to the reference's CPU decode). */
+cudaError_t qg_dequantize(int fmt, const uint8_t* payload, const uint8_t* meta,
+                          uint64_t first_block, uint64_t block_count, float* out,
+                          cudaStream_t stream);
+
+/* token = (argmax(values[0:n]) + token_offset + add_token * token) % modulus, the
+ * lowest index winning ties (argmax_token_kernel / output_token_sample_kernel,
+ * decode_kernels.cu:2993-3073).  add_token = 1, token_offset = 1, modulus = 32000
+ * reproduces the launchers' token update. */
+cudaError_t qg_argmax_token(const float* values, uint32_t n, uint32_t* token,
+                            uint32_t token_offset, uint32_t add_token, uint32_t modulus,
+                            cudaStream_t stream);
+
+/* Reads the library's device error word (QG_ERR_* bits) for the current device and
+ * clears it.  Synchronizes the device.  Returns the cudaError_t of the read. */
+cudaError_t qg_get_error(uint32_t* error_bits);
+
+/* Number of SMs and launch configuration the GEMV uses for a shape, for
+ * measurement code: grid CTAs, threads per CTA, rows per tile and pipeline stages. */
+cudaError_t qg_gemv_plan(int fmt, uint32_t rows, uint32_t cols, uint32_t* grid,
+                         uint32_t* threads, uint32_t* rows_per_tile, uint32_t* stages);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QGEMV_B200_H_ */

@@ -1,0 +1,220 @@
+// qg_aux.cu -- the small kernels around the GEMV: token argmax, the reference's
+// RMSNorm/SiLU feedback kernels, bit-exact dequantization, and the layer-slice
+// normalisation / gate kernels.
+#include <mutex>
+
+#include "qg_formats.cuh"
+#include "qg_host.h"
+
+namespace qg {
+
+// ---------------------------------------------------------------------------
+// argmax -> token.  Lowest index wins ties; NaN never wins; the running best
+// starts at -FLT_MAX with index 0, exactly like argmax_token_kernel /
+// output_token_sample_kernel (decode_kernels.cu:2993-3073), so the selected index
+// is the same for every input.  One CTA of 1024 threads; 16-B loads when aligned.
+__device__ __forceinline__ void better(float& bv, uint32_t& bi, float v, uint32_t i) {
+  if (v > bv || (v == bv && i < bi)) {
+    bv = v;
+    bi = i;
+  }
+}
+
+__global__ void __launch_bounds__(1024) argmax_token_kernel(const float* __restrict__ v,
+                                                            uint32_t n, uint32_t* token,
+                                                            uint32_t offset, uint32_t add_token,
+                                                            uint32_t modulus) {
+  __shared__ float sv[32];
+  __shared__ uint32_t si[32];
+  float bv = -3.4028234663852886e38f;
+  uint32_t bi = 0u;
+  const uint32_t tid = threadIdx.x;
+  uint32_t head = 0u;
+  if ((reinterpret_cast<uintptr_t>(v) & 15u) == 0u) {
+    const uint32_t n4 = n >> 2;
+    const float4* v4 = reinterpret_cast<const float4*>(v);
+    for (uint32_t j = tid; j < n4; j += blockDim.x) {
+      const float4 q = __ldg(v4 + j);
+      better(bv, bi, q.x, 4u * j);
+      better(bv, bi, q.y, 4u * j + 1u);
+      better(bv, bi, q.z, 4u * j + 2u);
+      better(bv, bi, q.w, 4u * j + 3u);
+    }
+    head = n4 << 2;
+  }
+  for (uint32_t i = head + tid; i < n; i += blockDim.x) better(bv, bi, __ldg(v + i), i);
+  for (int off = 16; off > 0; off >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+    const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, off);
+    better(bv, bi, ov, oi);
+  }
+  if ((tid & 31u) == 0u) {
+    sv[tid >> 5] = bv;
+    si[tid >> 5] = bi;
+  }
+  __syncthreads();
+  if (tid < 32u) {
+    const uint32_t nw = blockDim.x >> 5;
+    bv = tid < nw ? sv[tid] : -3.4028234663852886e38f;
+    bi = tid < nw ? si[tid] : 0u;
+    for (int off = 16; off > 0; off >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+      const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, off);
+      better(bv, bi, ov, oi);
+    }
+    if (tid == 0u) {
+      const uint32_t prev = add_token ? token[0] : 0u;
+      token[0] = (bi + prev + offset) % modulus;
+    }
+  }
+}
+
+cudaError_t launch_argmax_token(const float* v, uint32_t n, uint32_t* token, uint32_t offset,
+                                uint32_t add_token, uint32_t modulus, cudaStream_t stream) {
+  argmax_token_kernel<<<1, 1024, 0, stream>>>(v, n, token, offset, add_token, modulus);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Block-wide sum of squares of logits[0:rows] (every CTA computes it; rows is a
+// stage's output length, a few thousand floats read from L2).
+__device__ float block_sum_sq(const float* __restrict__ logits, uint32_t rows) {
+  __shared__ float ws[32];
+  float s = 0.f;
+  for (uint32_t r = threadIdx.x; r < rows; r += blockDim.x) {
+    const float v = __ldg(logits + r);
+    s += v * v;
+  }
+  for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+  if ((threadIdx.x & 31u) == 0u) ws[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x < 32u) {
+    s = threadIdx.x < (blockDim.x >> 5) ? ws[threadIdx.x] : 0.f;
+    for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+    if (threadIdx.x == 0u) ws[0] = s;
+  }
+  __syncthreads();
+  const float total = ws[0];
+  __syncthreads();
+  return total;
+}
+
+__device__ __forceinline__ float silu(float v) { return v * (1.0f / (1.0f + expf(-v))); }
+
+// The reference's feedback kernels (decode_kernels.cu:122-289), one kernel with a
+// mode switch; the RMS is computed once per CTA instead of once per thread.
+enum FeedbackMode : uint32_t {
+  kRmsnorm = 0,           // act[c] = n
+  kSiluRmsnorm = 1,       // act[c] = silu(n)
+  kRmsnormSiluCache = 2,  // act[c] = n, cache[c] = silu(n)
+  kGatedSilu = 3,         // act[c] = cache[c % cache_cols] * n
+  kCache = 4,             // cache[c] = (acc ? cache[c] : 0) + n
+  kSiluCache = 5,         // cache[c] = (acc ? cache[c] : 0) + silu(n)
+  kCacheGatedProduct = 6  // up[c] = (acc ? up[c] : 0) + n; act[c] = gate[c] * up[c]
+};
+
+__global__ void __launch_bounds__(256) feedback_kernel(uint32_t mode, const float* logits,
+                                                       float* act, float* cache,
+                                                       const float* gate, uint32_t rows,
+                                                       uint32_t cols, uint32_t cache_cols,
+                                                       float eps, uint32_t accumulate) {
+  const float sum_sq = block_sum_sq(logits, rows);
+  const float inv = 1.0f / sqrtf(sum_sq / static_cast<float>(rows) + eps);
+  const uint32_t c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= cols) return;
+  const float n = logits[c % rows] * inv;
+  switch (mode) {
+    case kRmsnorm: act[c] = n; break;
+    case kSiluRmsnorm: act[c] = silu(n); break;
+    case kRmsnormSiluCache: act[c] = n; cache[c] = silu(n); break;
+    case kGatedSilu: act[c] = cache[c % cache_cols] * n; break;
+    case kCache: cache[c] = accumulate ? cache[c] + n : n; break;
+    case kSiluCache: cache[c] = accumulate ? cache[c] + silu(n) : silu(n); break;
+    case kCacheGatedProduct: {
+      const float up = accumulate ? cache[c] + n : n;
+      cache[c] = up;
+      act[c] = gate[c] * up;
+      break;
+    }
+    default: break;
+  }
+}
+
+cudaError_t launch_feedback(uint32_t mode, const float* logits, float* act, float* cache,
+                            const float* gate, uint32_t rows, uint32_t cols, uint32_t cache_cols,
+                            float eps, uint32_t accumulate, cudaStream_t stream) {
+  if (rows == 0u || cols == 0u) return cudaSuccess;  // the reference kernels return early
+  const uint32_t blocks = (cols + 255u) / 256u;
+  feedback_kernel<<<blocks, 256, 0, stream>>>(mode, logits, act, cache, gate, rows, cols,
+                                              cache_cols, eps, accumulate);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Bit-exact dequantization (one thread per value).
+template <int FMT>
+__global__ void dequant_kernel(const uint8_t* payload, const uint8_t* meta, uint64_t first_block,
+                               uint64_t count, float* out) {
+  const uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= count * 256u) return;
+  out[i] = dequant_value<FMT>(payload, meta, first_block + (i >> 8), static_cast<uint32_t>(i & 255u));
+}
+
+cudaError_t launch_dequant(int fmt, const uint8_t* payload, const uint8_t* meta,
+                           uint64_t first_block, uint64_t count, float* out, cudaStream_t stream) {
+  const uint64_t total = count * 256u;
+  const uint32_t blocks = static_cast<uint32_t>((total + 255u) / 256u);
+  switch (fmt) {
+#define QG_DQ(F) \
+  case F: dequant_kernel<F><<<blocks, 256, 0, stream>>>(payload, meta, first_block, count, out); break;
+    QG_DQ(QG_FMT_Q4K_RAW)
+    QG_DQ(QG_FMT_Q4K_SPLIT_PREDECODED)
+    QG_DQ(QG_FMT_Q4K_SPLIT_HALF)
+    QG_DQ(QG_FMT_Q4K_SPLIT_COMPACT)
+    QG_DQ(QG_FMT_Q4K_SPLIT_NATIVE)
+    QG_DQ(QG_FMT_Q5K)
+    QG_DQ(QG_FMT_IQ2S)
+    QG_DQ(QG_FMT_IQ3S)
+#undef QG_DQ
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Layer-slice helpers (no reference counterpart): weighted RMSNorm and SiLU gate.
+
+// y = x / sqrt(mean(x^2) + eps) * w   (one CTA; n is the hidden size)
+__global__ void __launch_bounds__(1024) weighted_rmsnorm_kernel(const float* x, const float* w,
+                                                                uint32_t n, float eps, float* y) {
+  const float sum_sq = block_sum_sq(x, n);
+  const float inv = 1.0f / sqrtf(sum_sq / static_cast<float>(n) + eps);
+  for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) y[i] = x[i] * inv * w[i];
+}
+
+cudaError_t launch_weighted_rmsnorm(const float* x, const float* w, uint32_t n, float eps,
+                                    float* y, cudaStream_t stream) {
+  weighted_rmsnorm_kernel<<<1, 1024, 0, stream>>>(x, w, n, eps, y);
+  return cudaGetLastError();
+}
+
+// h = silu(gate) * up
+__global__ void silu_gate_kernel(const float* gate, const float* up, uint32_t n, float* h) {
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) h[i] = silu(gate[i]) * up[i];
+}
+
+cudaError_t launch_silu_gate(const float* gate, const float* up, uint32_t n, float* h,
+                             cudaStream_t stream) {
+  silu_gate_kernel<<<(n + 255u) / 256u, 256, 0, stream>>>(gate, up, n, h);
+  return cudaGetLastError();
+}
+
+int device_sm_count() {
+  int dev = 0, sms = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return sms;
+}
+
+}  // namespace qg

@@ -1,0 +1,46 @@
+// qg_host.h -- host-side interfaces shared by the library's translation units.
+#pragma once
+
+#include <cuda_runtime_api.h>
+#include <stdint.h>
+
+#include "../../include/qgemv_b200.h"
+
+namespace qg {
+
+// Launch configuration of the tiled GEMV for one shape (see qg_gemv.cu).
+struct GemvPlan {
+  uint32_t grid, threads, group, rpp, passes, rows_per_tile, num_tiles, stages;
+  uint32_t stage_bytes, meta_off, red_off, table_off, stage_off, smem_bytes;
+};
+
+GemvPlan plan_gemv(int fmt, uint32_t rows, uint32_t cols, int sms);
+
+// y = W x (+ residual); optional reference KV page write with the token read on
+// the device before the launch's first row is stored.
+cudaError_t launch_gemv(int fmt, const uint8_t* payload, const uint8_t* meta, const float* x,
+                        float* y, const float* residual, float* kv, const uint32_t* token,
+                        uint64_t kv_words, uint32_t page_words, uint32_t active_pages,
+                        uint32_t rows, uint32_t cols, cudaStream_t stream);
+
+// token = (argmax(v[0:n]) + offset + add_token * token) % modulus (one CTA).
+cudaError_t launch_argmax_token(const float* v, uint32_t n, uint32_t* token, uint32_t offset,
+                                uint32_t add_token, uint32_t modulus, cudaStream_t stream);
+
+// The reference's feedback kernels (modes in qg_aux.cu).
+cudaError_t launch_feedback(uint32_t mode, const float* logits, float* act, float* cache,
+                            const float* gate, uint32_t rows, uint32_t cols, uint32_t cache_cols,
+                            float eps, uint32_t accumulate, cudaStream_t stream);
+
+cudaError_t launch_dequant(int fmt, const uint8_t* payload, const uint8_t* meta,
+                           uint64_t first_block, uint64_t count, float* out, cudaStream_t stream);
+
+cudaError_t launch_weighted_rmsnorm(const float* x, const float* w, uint32_t n, float eps,
+                                    float* y, cudaStream_t stream);
+
+cudaError_t launch_silu_gate(const float* gate, const float* up, uint32_t n, float* h,
+                             cudaStream_t stream);
+
+int device_sm_count();
+
+}  // namespace qg
