@@ -46,7 +46,7 @@ CONFIG = {
                 "{4096x4096,14336x4096,4096x14336,128256x8192} (out x in), 16 GEMVs per step",
     "batch": 1,
     "l2": "no flush: 2.37 GB of packs streamed per step (> 126 MB L2)",
-    "entry_point": "qg_gemv (C-ABI)",
+    "entry_point": "qg_act_prepare once per distinct x + qg_gemv_act per GEMV (C-ABI), one CUDA graph per step",
 }
 
 
@@ -193,47 +193,69 @@ def run_ours(args) -> int:
     # Resident packs + activations (setup, untimed).
     mats = []
     xs = {}
-    for fmt in SWEEP_FORMATS:
-        for rows, cols in SWEEP_SHAPES:
-            pk = packs.synthetic_pack(fmt, rows, cols, seed=1000 * fmt + rows + cols)
-            payload, meta = ops.to_device(pk, device)
-            if cols not in xs:
-                xs[cols] = torch.from_numpy(packs.synthetic_activation(cols, cols)).to(device)
-            y = torch.empty(rows, dtype=torch.float32, device=device)
-            mats.append({"fmt": fmt, "rows": rows, "cols": cols, "payload": payload, "meta": meta,
-                         "y": y, "bytes": algorithmic_bytes(fmt, rows, cols)})
-            del pk
+    cases = [(f, r, c) for f in SWEEP_FORMATS for r, c in SWEEP_SHAPES]
+    if args.only:
+        f, shape = args.only.split(":")
+        r, c = shape.lower().split("x")
+        cases = [(int(f), int(r), int(c))]
+    for fmt, rows, cols in cases:
+        pk = packs.synthetic_pack(fmt, rows, cols, seed=1000 * fmt + rows + cols)
+        payload, meta = ops.to_device(pk, device)
+        if cols not in xs:
+            xs[cols] = torch.from_numpy(packs.synthetic_activation(cols, cols)).to(device)
+        y = torch.empty(rows, dtype=torch.float32, device=device)
+        mats.append({"fmt": fmt, "rows": rows, "cols": cols, "payload": payload, "meta": meta,
+                     "y": y, "bytes": algorithmic_bytes(fmt, rows, cols)})
+        del pk
     stream = torch.cuda.current_stream(device)
-    sh = stream.cuda_stream
 
-    def launch(m, x):
-        check("qg_gemv", m["fmt"], m["payload"].data_ptr(),
-              None if m["meta"] is None else m["meta"].data_ptr(), x.data_ptr(),
-              m["y"].data_ptr(), m["rows"], m["cols"], sh)
+    acts = {c: torch.empty(ops.act_bytes(c), dtype=torch.uint8, device=device) for c in xs}
+
+    def launch(m, x, act):
+        check("qg_gemv_act", m["fmt"], m["payload"].data_ptr(),
+              None if m["meta"] is None else m["meta"].data_ptr(), x.data_ptr(), act.data_ptr(),
+              m["y"].data_ptr(), m["rows"], m["cols"], torch.cuda.current_stream().cuda_stream)
 
     def step(events=None):
+        # Each distinct x is prepared once (int8 planes), then read by every GEMV on it.
+        for c in xs:
+            check("qg_act_prepare", xs[c].data_ptr(), c, acts[c].data_ptr(),
+                  torch.cuda.current_stream().cuda_stream)
+        if events is not None:
+            events[0].record()
         for i, m in enumerate(mats):
-            launch(m, xs[m["cols"]])
+            launch(m, xs[m["cols"]], acts[m["cols"]])
             if events is not None:
-                events[i + 1].record(stream)
+                events[i + 1].record()
 
-    for _ in range(max(3, args.warmup)):
+    for _ in range(max(3, args.warmup)):  # eager warm-up: sets kernel attributes, fills caches
         step()
+    torch.cuda.synchronize()
+
+    # One CUDA graph per timed step (16 GEMV nodes + 17 event-record nodes), the way
+    # the reference replays its decode step; distinct graphs keep every step's events.
+    graphs, evs = [], []
+    for _ in range(args.steps + max(3, args.warmup)):
+        ev = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(len(mats) + 1)]
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            step(ev)
+        graphs.append(g)
+        evs.append(ev)
+    warm = len(graphs) - args.steps
+    for g in graphs[:warm]:
+        g.replay()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
 
-    # Timed region: K steps, an event after every GEMV (per-kernel durations).
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(len(mats) + 1)] for _ in range(args.steps)]
-    torch.cuda.synchronize()
     with ClockSampler(local) as clocks:
         time.sleep(0.4)
         t_begin = torch.cuda.Event(enable_timing=True)
         t_end = torch.cuda.Event(enable_timing=True)
         t_begin.record(stream)
-        for k in range(args.steps):
-            evs[k][0].record(stream)
-            step(evs[k])
+        for g in graphs[warm:]:
+            g.replay()
         t_end.record(stream)
         torch.cuda.synchronize()
     elapsed_ms = t_begin.elapsed_time(t_end)
@@ -246,15 +268,16 @@ def run_ours(args) -> int:
     value = world * bytes_per_step * args.steps / (elapsed_ms * 1e-3) / 1e9
 
     per = []
+    timed = evs[warm:]
     for i, m in enumerate(mats):
-        ms = statistics.mean(evs[k][i].elapsed_time(evs[k][i + 1]) for k in range(args.steps))
+        ms = statistics.mean(timed[k][i].elapsed_time(timed[k][i + 1]) for k in range(args.steps))
         per.append({"format": packs.FORMAT_NAMES[m["fmt"]], "rows": m["rows"], "cols": m["cols"],
                     "ms": ms, "GBps": m["bytes"] / (ms * 1e-3) / 1e9})
     peak, peak_src = measured_peak()
     dom = max(range(len(mats)), key=lambda i: per[i]["ms"])
     dm = mats[dom]
     roofline = {
-        "bound": "hbm", "kernel": f"gemv_kernel<{packs.FORMAT_NAMES[dm['fmt']]}> {dm['rows']}x{dm['cols']}",
+        "bound": "hbm", "kernel": f"gemv_tiled_kernel<{packs.FORMAT_NAMES[dm['fmt']]}> {dm['rows']}x{dm['cols']}",
         "achieved": per[dom]["GBps"], "peak": peak, "unit": "GB/s",
         "frac": per[dom]["GBps"] / peak, "peak_source": peak_src,
         "algorithmic_bytes_per_launch": dm["bytes"], "traffic": None,
@@ -262,17 +285,21 @@ def run_ours(args) -> int:
     for row in per:
         row["frac_of_peak"] = row["GBps"] / peak
 
-    # End to end through the C-ABI: x from pinned host memory, y back, every step.
+    # End to end through the C-ABI: every step copies each GEMV's x from pinned host
+    # memory, replays the step graph, and copies every y back to pinned host memory.
     host_x = {c: xs[c].cpu().pin_memory() for c in xs}
     host_y = [torch.empty(m["rows"], dtype=torch.float32).pin_memory() for m in mats]
-    dev_x = [torch.empty(m["cols"], dtype=torch.float32, device=device) for m in mats]
-    h2d = sum(4 * m["cols"] for m in mats)
+    h2d = sum(4 * c for c in xs)
     d2h = sum(4 * m["rows"] for m in mats)
+    step_graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(step_graph):
+        step()
 
     def e2e_step():
+        for c in xs:  # the step's inputs: one host copy per distinct x
+            xs[c].copy_(host_x[c], non_blocking=True)
+        step_graph.replay()
         for i, m in enumerate(mats):
-            dev_x[i].copy_(host_x[m["cols"]], non_blocking=True)
-            launch(m, dev_x[i])
             host_y[i].copy_(m["y"], non_blocking=True)
 
     for _ in range(max(3, args.warmup)):
@@ -293,10 +320,11 @@ def run_ours(args) -> int:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t.item())
     e2e_value = world * bytes_per_step * args.steps / (e2e_ms * 1e-3) / 1e9
+    del graphs, step_graph
 
     err = ops.get_error()
     if rank == 0:
-        cpu = cpu_reference_sample(8, os.cpu_count() or 1) if world == 1 else None
+        cpu = cpu_reference_sample(8, os.cpu_count() or 1) if world == 1 and not args.only else None
         line = {
             "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup,
@@ -308,7 +336,7 @@ def run_ours(args) -> int:
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
-            "gpu_launches": len(mats) * args.steps,
+            "gpu_launches": (len(mats) + len(xs)) * args.steps,
             "clocks": clocks.summary(),
             "error_word": err,
             "per_matvec": per,
@@ -326,6 +354,9 @@ def main() -> int:
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--only", default=None,
+                    help="profiling case: run a single GEMV FMT:ROWSxCOLS (e.g. 0:32768x8192) "
+                         "instead of the sweep; skips the CPU baseline")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)

@@ -217,6 +217,18 @@ cudaError_t rtxllm_launch_rmsnorm_cache_and_gated_product(
 cudaError_t qg_gemv(int fmt, const uint8_t* payload, const uint8_t* meta, const float* x,
                     float* y, uint32_t rows, uint32_t cols, cudaStream_t stream);
 
+/* Prepared activations.  Every GEMV CTA needs x as two int8 planes per 32 columns
+ * (x ~= s * (hi + lo / 256), |error| <= 3.2e-5 * ||x||_inf).  qg_act_prepare computes
+ * them once into `act` (qg_act_bytes(cols) bytes, 16-B aligned, caller-owned) so the
+ * GEMVs that read the same x skip that work; qg_gemv does it inside the kernel. */
+cudaError_t qg_act_bytes(uint32_t cols, size_t* bytes);
+cudaError_t qg_act_prepare(const float* x, uint32_t cols, void* act, cudaStream_t stream);
+
+/* qg_gemv reading x through a prepared activation of the same x (act may be NULL). */
+cudaError_t qg_gemv_act(int fmt, const uint8_t* payload, const uint8_t* meta, const float* x,
+                        const void* act, float* y, uint32_t rows, uint32_t cols,
+                        cudaStream_t stream);
+
 /* One decode stage with the reference launchers' semantics (decode_kernels.cu:
  * 4032-4177): y for rows [0, rows), KV page write with the pre-update token for
  * rows < active_pages (kv may be NULL), then

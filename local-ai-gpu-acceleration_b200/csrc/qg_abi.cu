@@ -24,7 +24,7 @@ cudaError_t decode_stage(int fmt, const uint8_t* payload, const uint8_t* meta, c
                          float* y, float* kv, uint32_t* token, uint32_t rows, uint32_t cols,
                          uint32_t kv_words, uint32_t page_words, uint32_t active_pages,
                          cudaStream_t stream) {
-  cudaError_t e = qg::launch_gemv(fmt, payload, meta, x, y, nullptr, kv, token, kv_words,
+  cudaError_t e = qg::launch_gemv(fmt, payload, meta, x, nullptr, y, nullptr, kv, token, kv_words,
                                   page_words, active_pages, rows, cols, stream);
   if (e != cudaSuccess) return e;
   if (token == nullptr) return cudaSuccess;
@@ -227,8 +227,8 @@ static bool gemv_args_ok(int fmt, const uint8_t* payload, const uint8_t* meta, c
 cudaError_t qg_gemv(int fmt, const uint8_t* payload, const uint8_t* meta, const float* x, float* y,
                     uint32_t rows, uint32_t cols, cudaStream_t stream) {
   if (!gemv_args_ok(fmt, payload, meta, x, y, rows, cols)) return cudaErrorInvalidValue;
-  return qg::launch_gemv(fmt, payload, meta, x, y, nullptr, nullptr, nullptr, 0u, 0u, 0u, rows,
-                         cols, stream);
+  return qg::launch_gemv(fmt, payload, meta, x, nullptr, y, nullptr, nullptr, nullptr, 0u, 0u, 0u,
+                         rows, cols, stream);
 }
 
 cudaError_t qg_decode_stage(int fmt, const uint8_t* payload, const uint8_t* meta, const float* x,
@@ -250,11 +250,36 @@ cudaError_t qg_gemv_batched(int fmt, const uint8_t* payload, const uint8_t* meta
   }
   for (uint32_t b = 0; b < batch; ++b) {
     const cudaError_t e = qg::launch_gemv(fmt, payload, meta, x + static_cast<uint64_t>(b) * cols,
-                                          y + static_cast<uint64_t>(b) * rows, nullptr, nullptr,
-                                          nullptr, 0u, 0u, 0u, rows, cols, stream);
+                                          nullptr, y + static_cast<uint64_t>(b) * rows, nullptr,
+                                          nullptr, nullptr, 0u, 0u, 0u, rows, cols, stream);
     if (e != cudaSuccess) return e;
   }
   return cudaSuccess;
+}
+
+cudaError_t qg_act_bytes(uint32_t cols, size_t* bytes) {
+  if (bytes == nullptr || cols == 0u || (cols % 256u) != 0u) return cudaErrorInvalidValue;
+  *bytes = qg::act_bytes(cols);
+  return cudaSuccess;
+}
+
+cudaError_t qg_act_prepare(const float* x, uint32_t cols, void* act, cudaStream_t stream) {
+  if (x == nullptr || act == nullptr || cols == 0u || (cols % 256u) != 0u ||
+      (reinterpret_cast<uintptr_t>(act) & 15u) != 0u) {
+    return cudaErrorInvalidValue;
+  }
+  return qg::launch_act_prepare(x, cols, act, stream);
+}
+
+cudaError_t qg_gemv_act(int fmt, const uint8_t* payload, const uint8_t* meta, const float* x,
+                        const void* act, float* y, uint32_t rows, uint32_t cols,
+                        cudaStream_t stream) {
+  if (!gemv_args_ok(fmt, payload, meta, x, y, rows, cols) ||
+      (act != nullptr && (reinterpret_cast<uintptr_t>(act) & 15u) != 0u)) {
+    return cudaErrorInvalidValue;
+  }
+  return qg::launch_gemv(fmt, payload, meta, x, act, y, nullptr, nullptr, nullptr, 0u, 0u, 0u,
+                         rows, cols, stream);
 }
 
 cudaError_t qg_dequantize(int fmt, const uint8_t* payload, const uint8_t* meta,

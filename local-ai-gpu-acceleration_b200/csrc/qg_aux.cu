@@ -210,6 +210,26 @@ cudaError_t launch_silu_gate(const float* gate, const float* up, uint32_t n, flo
   return cudaGetLastError();
 }
 
+// ---------------------------------------------------------------------------
+// Activation preparation: x -> one ActChunk (int8 planes + scales + sums) per 64
+// columns, read by every GEMV CTA instead of re-quantizing x in each of them.
+__global__ void act_prepare_kernel(const float* __restrict__ x, uint32_t chunks, ActChunk* out,
+                                   uint32_t x_vec) {
+  const uint32_t c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= chunks) return;
+  XChunk xr;
+  load_x_chunk(x + 64u * c, x_vec != 0u, xr);
+  store_act_chunk(xr, out + c);
+}
+
+cudaError_t launch_act_prepare(const float* x, uint32_t cols, void* act, cudaStream_t stream) {
+  const uint32_t chunks = cols / 64u;
+  const uint32_t vec = (reinterpret_cast<uintptr_t>(x) & 15u) == 0u ? 1u : 0u;
+  act_prepare_kernel<<<(chunks + 63u) / 64u, 64, 0, stream>>>(x, chunks,
+                                                              static_cast<ActChunk*>(act), vec);
+  return cudaGetLastError();
+}
+
 int device_sm_count() {
   int dev = 0, sms = 0;
   cudaGetDevice(&dev);

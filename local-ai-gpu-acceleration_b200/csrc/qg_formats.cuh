@@ -6,14 +6,11 @@
 //    device twins decode_kernels.cu:1504-1728) with explicit _rn operations so
 //    nvcc cannot contract them -- bit-identical fp32 output.
 //  * chunk_dot<FMT>: the GEMV inner product of one 64-column chunk of one row,
-//    reading the row's bytes from shared memory.  It uses the factorised form
-//    sum_sub (d*scale) * sum(q*x) - (dmin*min) * sum(x) with packed f32x2 FMAs, so
-//    it agrees with the reference within fp32 reassociation error.
+//    reading the row's bytes from shared memory (see the GEMV section below).
 //
 // A 64-column chunk c of a row covers columns [64c, 64c+64): for the K-quants the
 // low/high nibbles of qs[32*(c%4) .. +32) of block c/4, for the IQ formats the two
-// 32-value sub-blocks 2*(c%4), 2*(c%4)+1 of block c/4.  The thread that owns chunk c
-// keeps x[64c .. 64c+64) in registers as xa (first 32) and xb (last 32).
+// 32-value sub-blocks 2*(c%4), 2*(c%4)+1 of block c/4.
 #pragma once
 
 #include "qg_common.cuh"
@@ -165,69 +162,172 @@ __device__ __forceinline__ float dequant_value<QG_FMT_IQ3S>(const uint8_t* paylo
 }
 
 // ---------------------------------------------------------------------------
-// GEMV chunk readers (shared memory).
+// GEMV chunk readers (shared memory), integer dot products.
+//
+// x is held by each thread as two signed-byte planes per 32-column half:
+//   x_j ~= s * (hi_j + lo_j / 256),  s = max|x| / 126 over the half,
+// |error| <= s / 256 <= 3.2e-5 * ||x||_inf per element, i.e. <= 3.2e-5 *
+// ||w_row||_1 * ||x||_inf per output -- 30x inside the 1e-3 parity bound.  Every
+// format is decoded to small non-negative integers u (bytes) so one dp4a handles
+// four weights per plane:
+//   Q4_K/Q5_K  u = q (4/5-bit quant);   row sum = d*sc*sum(q x) - dmin*m*sum(x)
+//   IQ2_S      u = v + 8  = 2k XOR (sign ? 7 : 9)       (v = +-(2k+1))
+//   IQ3_S      u = v + 15 = g  XOR (sign ? 0x0F : 0x11) (v = +-g, g odd <= 15)
+// the IQ biases are removed with per-16-column sums of the x planes.
 
-struct ChunkX {
-  float2 a[16];  // x[64c + 0 .. 31]
-  float2 b[16];  // x[64c + 32 .. 63]
-  float sa, sb;  // sum of a, sum of b
+struct XChunk {
+  uint32_t ah[8], al[8];  // half A (columns 0..31): hi / lo planes, word i = columns 4i..4i+3
+  uint32_t bh[8], bl[8];  // half B (columns 32..63)
+  float sa, sb;           // plane scales of the halves
+  float suma, sumb;       // exact fp32 sums of x over the halves
+  int qh[4], ql[4];       // plane byte sums per 16-column quarter (IQ bias removal)
 };
 
-// sum_j q_j * x_j over 32 values for the low (A) and high (B) 4/5-bit fields held
-// as bytes of lo[i]/hi[i] (value 4i+k in byte k).  Exact small integers are made
-// with the 2^23 magic-number trick; f32x2 FMAs accumulate.
-__device__ __forceinline__ void byte_field_dot(const uint32_t (&lo)[8], const uint32_t (&hi)[8],
-                                               const ChunkX& x, float& sA, float& sB) {
-  const float2 mg = make_float2(-kMagic, -kMagic);
-  float2 a0 = make_float2(0.f, 0.f), a1 = a0, b0 = a0, b1 = a0;
+__device__ __forceinline__ void quantize_half(const float (&v)[32], uint32_t (&hi)[8],
+                                              uint32_t (&lo)[8], float& s, float& sum,
+                                              int& qh0, int& ql0, int& qh1, int& ql1) {
+  float m = 0.f, t = 0.f;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    m = fmaxf(m, fabsf(v[j]));
+    t += v[j];
+  }
+  sum = t;
+  s = m > 0.f ? m * (1.0f / 126.0f) : 1.0f;
+  const float inv = 1.0f / s;
+  // Round to nearest even with the 1.5 * 2^23 magic number: for |u| < 2^22 the low
+  // mantissa bits of u + 1.5*2^23 hold round(u) as a two's-complement integer.
+  constexpr float kRound = 12582912.0f;
+  constexpr int kRoundBits = 0x4b400000;
+  qh0 = ql0 = qh1 = ql1 = 0;
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
-    const float2 l01 = __fadd2_rn(make_float2(byte_magic(lo[i], 0), byte_magic(lo[i], 1)), mg);
-    const float2 l23 = __fadd2_rn(make_float2(byte_magic(lo[i], 2), byte_magic(lo[i], 3)), mg);
-    const float2 h01 = __fadd2_rn(make_float2(byte_magic(hi[i], 0), byte_magic(hi[i], 1)), mg);
-    const float2 h23 = __fadd2_rn(make_float2(byte_magic(hi[i], 2), byte_magic(hi[i], 3)), mg);
-    a0 = __ffma2_rn(l01, x.a[2 * i], a0);
-    a1 = __ffma2_rn(l23, x.a[2 * i + 1], a1);
-    b0 = __ffma2_rn(h01, x.b[2 * i], b0);
-    b1 = __ffma2_rn(h23, x.b[2 * i + 1], b1);
+    int ia[4], ib[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float u = v[4 * i + k] * inv;
+      const float ur = u + kRound;
+      ia[k] = __float_as_int(ur) - kRoundBits;
+      const float r = (u - (ur - kRound)) * 256.0f;
+      ib[k] = min(max(__float_as_int(r + kRound) - kRoundBits, -127), 127);
+    }
+    hi[i] = __byte_perm(__byte_perm(ia[0], ia[1], 0x0040), __byte_perm(ia[2], ia[3], 0x0040), 0x5410);
+    lo[i] = __byte_perm(__byte_perm(ib[0], ib[1], 0x0040), __byte_perm(ib[2], ib[3], 0x0040), 0x5410);
+    const int sa = (ia[0] + ia[1]) + (ia[2] + ia[3]);
+    const int sb = (ib[0] + ib[1]) + (ib[2] + ib[3]);
+    if (i < 4) {
+      qh0 += sa;
+      ql0 += sb;
+    } else {
+      qh1 += sa;
+      ql1 += sb;
+    }
   }
-  sA = (a0.x + a0.y) + (a1.x + a1.y);
-  sB = (b0.x + b0.y) + (b1.x + b1.y);
 }
 
-// 32 packed Q4_K nibble bytes (two uint4) -> dot products of both nibble halves.
-__device__ __forceinline__ void q4_nibble_dot(const uint4 q0, const uint4 q1, const ChunkX& x,
+__device__ __forceinline__ int dp4a(uint32_t a, uint32_t b, int c) {
+  return __dp4a(static_cast<int>(a), static_cast<int>(b), c);
+}
+
+// dot of 4 unsigned bytes of a with 4 signed bytes of b, plus c.
+__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
+  int d;
+  asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
+// Exact int -> float for small magnitudes with full-rate ALU/FMA ops (no I2F):
+// u < 2^23 via the 2^23 magic number, |v| < 2^22 via 1.5 * 2^23.
+__device__ __forceinline__ float u2f_small(uint32_t u) {
+  return __uint_as_float(0x4b000000u | u) - 8388608.0f;
+}
+__device__ __forceinline__ float i2f_mid(int v) {
+  return __int_as_float(0x4b400000 + v) - 12582912.0f;
+}
+
+// s * (ih + il / 256)
+__device__ __forceinline__ float planes_value(int ih, int il, float s) {
+  return s * fmaf(i2f_mid(il), 0.00390625f, i2f_mid(ih));
+}
+
+// sum(q x) over both halves for 8 words of byte quants: A = lo[], B = hi[].
+__device__ __forceinline__ void quant_dot(const uint32_t (&lo)[8], const uint32_t (&hi)[8],
+                                          const XChunk& x, float& sA, float& sB) {
+  int ah0 = 0, al0 = 0, bh0 = 0, bl0 = 0, ah1 = 0, al1 = 0, bh1 = 0, bl1 = 0;
+#pragma unroll
+  for (int i = 0; i < 8; i += 2) {
+    ah0 = dp4a(lo[i], x.ah[i], ah0);
+    al0 = dp4a(lo[i], x.al[i], al0);
+    bh0 = dp4a(hi[i], x.bh[i], bh0);
+    bl0 = dp4a(hi[i], x.bl[i], bl0);
+    ah1 = dp4a(lo[i + 1], x.ah[i + 1], ah1);
+    al1 = dp4a(lo[i + 1], x.al[i + 1], al1);
+    bh1 = dp4a(hi[i + 1], x.bh[i + 1], bh1);
+    bl1 = dp4a(hi[i + 1], x.bl[i + 1], bl1);
+  }
+  sA = planes_value(ah0 + ah1, al0 + al1, x.sa);
+  sB = planes_value(bh0 + bh1, bl0 + bl1, x.sb);
+}
+
+// Q4_K: low nibbles are w & 0x0F0F0F0F; the high nibbles stay in place
+// (w & 0xF0F0F0F0 = 16 * q, unsigned bytes) and the 1/16 goes into the scale.
+__device__ __forceinline__ void q4_nibble_dot(const uint4 q0, const uint4 q1, const XChunk& x,
                                               float& sA, float& sB) {
   const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-  uint32_t lo[8], hi[8];
+  int ah0 = 0, al0 = 0, bh0 = 0, bl0 = 0, ah1 = 0, al1 = 0, bh1 = 0, bl1 = 0;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    lo[i] = w[i] & 0x0f0f0f0fu;
-    hi[i] = (w[i] >> 4u) & 0x0f0f0f0fu;
+  for (int i = 0; i < 8; i += 2) {
+    const uint32_t l0 = w[i] & 0x0f0f0f0fu, h0 = w[i] & 0xf0f0f0f0u;
+    const uint32_t l1 = w[i + 1] & 0x0f0f0f0fu, h1 = w[i + 1] & 0xf0f0f0f0u;
+    ah0 = dp4a(l0, x.ah[i], ah0);
+    al0 = dp4a(l0, x.al[i], al0);
+    bh0 = dp4a_us(h0, x.bh[i], bh0);
+    bl0 = dp4a_us(h0, x.bl[i], bl0);
+    ah1 = dp4a(l1, x.ah[i + 1], ah1);
+    al1 = dp4a(l1, x.al[i + 1], al1);
+    bh1 = dp4a_us(h1, x.bh[i + 1], bh1);
+    bl1 = dp4a_us(h1, x.bl[i + 1], bl1);
   }
-  byte_field_dot(lo, hi, x, sA, sB);
+  sA = planes_value(ah0 + ah1, al0 + al1, x.sa);
+  sB = planes_value(bh0 + bh1, bl0 + bl1, x.sb * 0.0625f);
 }
+
+// Shared-memory codebook tables of the IQ kernels.
+struct IqTables {
+  const uint2* kgrid2;  // IQ2_S: 1024 x 8 bytes 2k
+  const uint2* sign2;   // IQ2_S: 256 x 8 bytes (sign ? 0x0E : 0)
+  const uint32_t* grid3;  // IQ3_S: 512 x 4 magnitudes
+  const uint2* sign3;   // IQ3_S: 256 x 8 bytes (sign ? 0x1E : 0)
+};
 
 template <int FMT>
 __device__ __forceinline__ float chunk_dot(const uint8_t* rp, const uint8_t* rm, uint32_t c,
-                                           const ChunkX& x, const uint16_t* kgrid,
-                                           const uint32_t* grid3);
+                                           const XChunk& x, const IqTables& t);
 
-// Q4_K raw block header: d, dmin, scales -> the chunk's two (scale, min) products.
+// Q4_K 16-byte header {d, dmin, scales[12]} -> the chunk's row contribution.  Both
+// (scale, min) pairs 2g, 2g+1 of get_scale_min_k4 are unpacked two bytes at a time.
 __device__ __forceinline__ float q4k_header_combine(const uint4 h, uint32_t g, float sA, float sB,
-                                                    const ChunkX& x) {
+                                                    const XChunk& x) {
   const float d = h2f(h.x), dmin = h2f(h.x >> 16);
-  uint32_t sc0, m0, sc1, m1;
-  scale_min_k4(2u * g, h.y, h.z, h.w, sc0, m0);
-  scale_min_k4(2u * g + 1u, h.y, h.z, h.w, sc1, m1);
-  return d * (static_cast<float>(sc0) * sA + static_cast<float>(sc1) * sB) -
-         dmin * (static_cast<float>(m0) * x.sa + static_cast<float>(m1) * x.sb);
+  const uint32_t sh = 16u * (g & 1u);
+  const uint32_t y16 = (h.y >> sh) & 0xffffu, z16 = (h.z >> sh) & 0xffffu, w16 = (h.w >> sh) & 0xffffu;
+  uint32_t scp, mnp;
+  if (g < 2u) {
+    scp = y16 & 0x3f3fu;
+    mnp = z16 & 0x3f3fu;
+  } else {
+    scp = (w16 & 0x0f0fu) | ((y16 & 0xc0c0u) >> 2);
+    mnp = ((w16 >> 4) & 0x0f0fu) | ((z16 & 0xc0c0u) >> 2);
+  }
+  const float sc0 = u2f_small(scp & 0xffu), sc1 = u2f_small(scp >> 8);
+  const float m0 = u2f_small(mnp & 0xffu), m1 = u2f_small(mnp >> 8);
+  return d * (sc0 * sA + sc1 * sB) - dmin * (m0 * x.suma + m1 * x.sumb);
 }
 
 template <>
 __device__ __forceinline__ float chunk_dot<QG_FMT_Q4K_RAW>(const uint8_t* rp, const uint8_t*,
-                                                           uint32_t c, const ChunkX& x,
-                                                           const uint16_t*, const uint32_t*) {
+                                                           uint32_t c, const XChunk& x,
+                                                           const IqTables&) {
   const uint8_t* blk = rp + (c >> 2) * 144u;
   const uint32_t g = c & 3u;
   const uint4 h = *reinterpret_cast<const uint4*>(blk);
@@ -240,8 +340,7 @@ __device__ __forceinline__ float chunk_dot<QG_FMT_Q4K_RAW>(const uint8_t* rp, co
 
 template <>
 __device__ __forceinline__ float chunk_dot<QG_FMT_Q4K_SPLIT_NATIVE>(
-    const uint8_t* rp, const uint8_t* rm, uint32_t c, const ChunkX& x, const uint16_t*,
-    const uint32_t*) {
+    const uint8_t* rp, const uint8_t* rm, uint32_t c, const XChunk& x, const IqTables&) {
   const uint32_t b = c >> 2, g = c & 3u;
   const uint4 h = *reinterpret_cast<const uint4*>(rm + b * 16u);
   const uint4 q0 = *reinterpret_cast<const uint4*>(rp + b * 128u + 32u * g);
@@ -253,34 +352,31 @@ __device__ __forceinline__ float chunk_dot<QG_FMT_Q4K_SPLIT_NATIVE>(
 
 template <>
 __device__ __forceinline__ float chunk_dot<QG_FMT_Q4K_SPLIT_PREDECODED>(
-    const uint8_t* rp, const uint8_t* rm, uint32_t c, const ChunkX& x, const uint16_t*,
-    const uint32_t*) {
+    const uint8_t* rp, const uint8_t* rm, uint32_t c, const XChunk& x, const IqTables&) {
   const uint32_t b = c >> 2, g = c & 3u;
   const float4 sm = *reinterpret_cast<const float4*>(rm + b * 64u + 16u * g);
   const uint4 q0 = *reinterpret_cast<const uint4*>(rp + b * 128u + 32u * g);
   const uint4 q1 = *reinterpret_cast<const uint4*>(rp + b * 128u + 32u * g + 16u);
   float sA, sB;
   q4_nibble_dot(q0, q1, x, sA, sB);
-  return (sm.x * sA + sm.z * sB) - (sm.y * x.sa + sm.w * x.sb);
+  return (sm.x * sA + sm.z * sB) - (sm.y * x.suma + sm.w * x.sumb);
 }
 
 template <>
 __device__ __forceinline__ float chunk_dot<QG_FMT_Q4K_SPLIT_HALF>(
-    const uint8_t* rp, const uint8_t* rm, uint32_t c, const ChunkX& x, const uint16_t*,
-    const uint32_t*) {
+    const uint8_t* rp, const uint8_t* rm, uint32_t c, const XChunk& x, const IqTables&) {
   const uint32_t b = c >> 2, g = c & 3u;
   const uint2 hm = *reinterpret_cast<const uint2*>(rm + b * 32u + 8u * g);
   const uint4 q0 = *reinterpret_cast<const uint4*>(rp + b * 128u + 32u * g);
   const uint4 q1 = *reinterpret_cast<const uint4*>(rp + b * 128u + 32u * g + 16u);
   float sA, sB;
   q4_nibble_dot(q0, q1, x, sA, sB);
-  return (h2f(hm.x) * sA + h2f(hm.y) * sB) - (h2f(hm.x >> 16) * x.sa + h2f(hm.y >> 16) * x.sb);
+  return (h2f(hm.x) * sA + h2f(hm.y) * sB) - (h2f(hm.x >> 16) * x.suma + h2f(hm.y >> 16) * x.sumb);
 }
 
 template <>
 __device__ __forceinline__ float chunk_dot<QG_FMT_Q4K_SPLIT_COMPACT>(
-    const uint8_t* rp, const uint8_t* rm, uint32_t c, const ChunkX& x, const uint16_t*,
-    const uint32_t*) {
+    const uint8_t* rp, const uint8_t* rm, uint32_t c, const XChunk& x, const IqTables&) {
   const uint32_t b = c >> 2, g = c & 3u;
   const uint8_t* m = rm + b * 20u;
   const uint32_t dd = *reinterpret_cast<const uint32_t*>(m);
@@ -290,14 +386,14 @@ __device__ __forceinline__ float chunk_dot<QG_FMT_Q4K_SPLIT_COMPACT>(
   const uint4 q1 = *reinterpret_cast<const uint4*>(rp + b * 128u + 32u * g + 16u);
   float sA, sB;
   q4_nibble_dot(q0, q1, x, sA, sB);
-  return h2f(dd) * (static_cast<float>(sc & 0xffu) * sA + static_cast<float>(sc >> 8) * sB) -
-         h2f(dd >> 16) * (static_cast<float>(mn & 0xffu) * x.sa + static_cast<float>(mn >> 8) * x.sb);
+  return h2f(dd) * (u2f_small(sc & 0xffu) * sA + u2f_small(sc >> 8) * sB) -
+         h2f(dd >> 16) * (u2f_small(mn & 0xffu) * x.suma + u2f_small(mn >> 8) * x.sumb);
 }
 
 template <>
 __device__ __forceinline__ float chunk_dot<QG_FMT_Q5K>(const uint8_t* rp, const uint8_t*,
-                                                       uint32_t c, const ChunkX& x,
-                                                       const uint16_t*, const uint32_t*) {
+                                                       uint32_t c, const XChunk& x,
+                                                       const IqTables&) {
   const uint8_t* blk = rp + (c >> 2) * 176u;
   const uint32_t g = c & 3u;
   const uint4 h = *reinterpret_cast<const uint4*>(blk);
@@ -315,77 +411,53 @@ __device__ __forceinline__ float chunk_dot<QG_FMT_Q5K>(const uint8_t* rp, const 
     hi[i] = ((w[i] >> 4u) & 0x0f0f0f0fu) | (((hw[i] >> sh) & 0x01010101u) << 4u);
   }
   float sA, sB;
-  byte_field_dot(lo, hi, x, sA, sB);
+  quant_dot(lo, hi, x, sA, sB);
   return q4k_header_combine(h, g, sA, sB, x);
-}
-
-// sum_l sign_l * (2 k_l + 1) * x_l for one IQ2_S group of 8 values: kgrid entry G
-// (eight 2-bit k), sign byte S, x = four float2 (values 0..7).
-__device__ __forceinline__ float iq2_group_dot(uint32_t G, uint32_t S, const float2* xs) {
-  float2 acc = make_float2(0.f, 0.f);
-  const float2 mg = make_float2(-kMagic, -kMagic);
-#pragma unroll
-  for (int p = 0; p < 4; ++p) {
-    const uint32_t l0 = 2u * p, l1 = 2u * p + 1u;
-    const float m0 = __uint_as_float(0x4b000001u | (((G >> (2u * l0)) & 3u) << 1u));
-    const float m1 = __uint_as_float(0x4b000001u | (((G >> (2u * l1)) & 3u) << 1u));
-    const float2 m = __fadd2_rn(make_float2(m0, m1), mg);
-    const float x0 = __uint_as_float(__float_as_uint(xs[p].x) ^ (((S >> l0) & 1u) << 31u));
-    const float x1 = __uint_as_float(__float_as_uint(xs[p].y) ^ (((S >> l1) & 1u) << 31u));
-    acc = __ffma2_rn(m, make_float2(x0, x1), acc);
-  }
-  return acc.x + acc.y;
 }
 
 template <>
 __device__ __forceinline__ float chunk_dot<QG_FMT_IQ2S>(const uint8_t* rp, const uint8_t*,
-                                                        uint32_t c, const ChunkX& x,
-                                                        const uint16_t* kgrid, const uint32_t*) {
+                                                        uint32_t c, const XChunk& x,
+                                                        const IqTables& t) {
   const uint8_t* blk = rp + (c >> 2) * 82u;
   const uint32_t sub = c & 3u;
   const float d = h2f(ld_u16(blk));
-  const uint32_t gl0 = ld_u32_a2(blk + 2u + 8u * sub), gl1 = ld_u32_a2(blk + 6u + 8u * sub);
-  const uint32_t sg0 = ld_u32_a2(blk + 34u + 8u * sub), sg1 = ld_u32_a2(blk + 38u + 8u * sub);
+  const uint32_t gl[2] = {ld_u32_a2(blk + 2u + 8u * sub), ld_u32_a2(blk + 6u + 8u * sub)};
+  const uint32_t sg[2] = {ld_u32_a2(blk + 34u + 8u * sub), ld_u32_a2(blk + 38u + 8u * sub)};
   const uint32_t qh = ld_u16(blk + 66u + 2u * sub);
   const uint32_t sc = ld_u16(blk + 74u + 2u * sub);
   float res = 0.f;
 #pragma unroll
   for (int ib = 0; ib < 2; ++ib) {
-    const uint32_t gl = ib ? gl1 : gl0, sg = ib ? sg1 : sg0;
-    const uint32_t qhb = (qh >> (8u * ib)) & 0xffu, sb = (sc >> (8u * ib)) & 0xffu;
-    const float2* xs = ib ? x.b : x.a;
-    float p[4];
+    const uint32_t* H = ib ? x.bh : x.ah;
+    const uint32_t* Lp = ib ? x.bl : x.al;
+    const uint32_t qhb = (qh >> (8 * ib)) & 0xffu;
+    int ih[2] = {0, 0}, il[2] = {0, 0};
 #pragma unroll
     for (int g = 0; g < 4; ++g) {
-      const uint32_t idx = byte_of(gl, g) | ((qhb << (8u - 2u * g)) & 0x300u);
-      p[g] = iq2_group_dot(kgrid[idx], byte_of(sg, g), xs + 4 * g);
+      const uint32_t idx = byte_of(gl[ib], g) | ((qhb << (8 - 2 * g)) & 0x300u);
+      const uint2 k2 = t.kgrid2[idx];
+      const uint2 sm = t.sign2[byte_of(sg[ib], g)];
+      const uint32_t u0 = k2.x ^ sm.x ^ 0x09090909u;
+      const uint32_t u1 = k2.y ^ sm.y ^ 0x09090909u;
+      ih[g >> 1] = dp4a(u1, H[2 * g + 1], dp4a(u0, H[2 * g], ih[g >> 1]));
+      il[g >> 1] = dp4a(u1, Lp[2 * g + 1], dp4a(u0, Lp[2 * g], il[g >> 1]));
     }
-    const float s_lo = d * (0.5f + static_cast<float>(sb & 0x0fu)) * 0.25f;
-    const float s_hi = d * (0.5f + static_cast<float>(sb >> 4u)) * 0.25f;
-    res += s_lo * (p[0] + p[1]) + s_hi * (p[2] + p[3]);
+    const float s = ib ? x.sb : x.sa;
+    const float p0 = planes_value(ih[0] - 8 * x.qh[2 * ib], il[0] - 8 * x.ql[2 * ib], s);
+    const float p1 = planes_value(ih[1] - 8 * x.qh[2 * ib + 1], il[1] - 8 * x.ql[2 * ib + 1], s);
+    const uint32_t sb = (sc >> (8 * ib)) & 0xffu;
+    const float s_lo = d * (0.5f + u2f_small(sb & 0x0fu)) * 0.25f;
+    const float s_hi = d * (0.5f + u2f_small(sb >> 4u)) * 0.25f;
+    res += s_lo * p0 + s_hi * p1;
   }
   return res;
 }
 
-// sum over 4 values of sign * magnitude * x for one IQ3_S grid entry (4 byte
-// magnitudes), sign bits sbits (bit l for value l), x = two float2.
-__device__ __forceinline__ float iq3_quad_dot(uint32_t grid, uint32_t sbits, const float2* xs) {
-  const float2 mg = make_float2(-kMagic, -kMagic);
-  const float2 m01 = __fadd2_rn(make_float2(byte_magic(grid, 0), byte_magic(grid, 1)), mg);
-  const float2 m23 = __fadd2_rn(make_float2(byte_magic(grid, 2), byte_magic(grid, 3)), mg);
-  const float x0 = __uint_as_float(__float_as_uint(xs[0].x) ^ ((sbits & 1u) << 31u));
-  const float x1 = __uint_as_float(__float_as_uint(xs[0].y) ^ (((sbits >> 1u) & 1u) << 31u));
-  const float x2 = __uint_as_float(__float_as_uint(xs[1].x) ^ (((sbits >> 2u) & 1u) << 31u));
-  const float x3 = __uint_as_float(__float_as_uint(xs[1].y) ^ (((sbits >> 3u) & 1u) << 31u));
-  float2 acc = __ffma2_rn(m01, make_float2(x0, x1), make_float2(0.f, 0.f));
-  acc = __ffma2_rn(m23, make_float2(x2, x3), acc);
-  return acc.x + acc.y;
-}
-
 template <>
 __device__ __forceinline__ float chunk_dot<QG_FMT_IQ3S>(const uint8_t* rp, const uint8_t*,
-                                                        uint32_t c, const ChunkX& x,
-                                                        const uint16_t*, const uint32_t* grid3) {
+                                                        uint32_t c, const XChunk& x,
+                                                        const IqTables& t) {
   const uint8_t* blk = rp + (c >> 2) * 110u;
   const uint32_t sub = c & 3u;
   const float d = h2f(ld_u16(blk));
@@ -393,30 +465,157 @@ __device__ __forceinline__ float chunk_dot<QG_FMT_IQ3S>(const uint8_t* rp, const
 #pragma unroll
   for (int i = 0; i < 4; ++i) qs[i] = ld_u32_a2(blk + 2u + 16u * sub + 4u * i);
   const uint32_t qh = ld_u16(blk + 66u + 2u * sub);
-  const uint32_t sg0 = ld_u32_a2(blk + 74u + 8u * sub), sg1 = ld_u32_a2(blk + 78u + 8u * sub);
+  const uint32_t sg[2] = {ld_u32_a2(blk + 74u + 8u * sub), ld_u32_a2(blk + 78u + 8u * sub)};
   const uint32_t sb = blk[106u + sub];
   float res = 0.f;
 #pragma unroll
   for (int ib = 0; ib < 2; ++ib) {
-    const uint32_t qhb = (qh >> (8u * ib)) & 0xffu;
-    const uint32_t sg = ib ? sg1 : sg0;
-    const float2* xs = ib ? x.b : x.a;
-    float acc = 0.f;
+    const uint32_t* H = ib ? x.bh : x.ah;
+    const uint32_t* Lp = ib ? x.bl : x.al;
+    const uint32_t qhb = (qh >> (8 * ib)) & 0xffu;
+    int ih = 0, il = 0;
 #pragma unroll
     for (int g = 0; g < 4; ++g) {
-      const uint32_t sbyte = byte_of(sg, g);
+      const uint2 sm = t.sign3[byte_of(sg[ib], g)];
 #pragma unroll
       for (int p = 0; p < 2; ++p) {
-        const uint32_t sel = 2u * g + p;  // byte index within this sub-block's 8 qs bytes
-        const uint32_t qb = byte_of(qs[2 * ib + (sel >> 2)], sel & 3u);
-        const uint32_t idx = qb | (((qhb >> (2u * g + p)) & 1u) << 8u);
-        acc += iq3_quad_dot(grid3[idx], sbyte >> (4u * p), xs + 4 * g + 2 * p);
+        const int sel = 2 * g + p;
+        const uint32_t qb = byte_of(qs[2 * ib + (sel >> 2)], sel & 3);
+        const uint32_t idx = qb | (((qhb >> sel) & 1u) << 8u);
+        const uint32_t u = t.grid3[idx] ^ 0x11111111u ^ (p ? sm.y : sm.x);
+        ih = dp4a(u, H[sel], ih);
+        il = dp4a(u, Lp[sel], il);
       }
     }
+    const float s = ib ? x.sb : x.sa;
+    const float pv = planes_value(ih - 15 * (x.qh[2 * ib] + x.qh[2 * ib + 1]),
+                                  il - 15 * (x.ql[2 * ib] + x.ql[2 * ib + 1]), s);
     const uint32_t nib = ib ? (sb >> 4u) : (sb & 0x0fu);
-    res += d * static_cast<float>(1u + 2u * nib) * acc;
+    res += d * u2f_small(1u + 2u * nib) * pv;
   }
   return res;
+}
+
+// Build the IQ tables of a format into shared memory (all threads of the caller).
+template <int FMT>
+__device__ __forceinline__ void build_iq_tables(uint8_t* base, uint32_t tid, uint32_t n) {
+  if (FMT == QG_FMT_IQ2S) {
+    uint2* k2 = reinterpret_cast<uint2*>(base);
+    uint2* s2 = k2 + 1024;
+    for (uint32_t i = tid; i < 1024u; i += n) {
+      const uint32_t G = g_iq2s_kgrid[i];
+      uint32_t lo = 0u, hi = 0u;
+#pragma unroll
+      for (int l = 0; l < 4; ++l) {
+        lo |= (((G >> (2 * l)) & 3u) << 1) << (8 * l);
+        hi |= (((G >> (2 * (l + 4))) & 3u) << 1) << (8 * l);
+      }
+      k2[i] = make_uint2(lo, hi);
+    }
+    for (uint32_t i = tid; i < 256u; i += n) {
+      uint32_t lo = 0u, hi = 0u;
+#pragma unroll
+      for (int l = 0; l < 4; ++l) {
+        lo |= ((i >> l) & 1u ? 0x0eu : 0u) << (8 * l);
+        hi |= ((i >> (l + 4)) & 1u ? 0x0eu : 0u) << (8 * l);
+      }
+      s2[i] = make_uint2(lo, hi);
+    }
+  } else if (FMT == QG_FMT_IQ3S) {
+    uint32_t* g3 = reinterpret_cast<uint32_t*>(base);
+    uint2* s3 = reinterpret_cast<uint2*>(base + 2048);
+    for (uint32_t i = tid; i < 512u; i += n) g3[i] = g_iq3s_grid[i];
+    for (uint32_t i = tid; i < 256u; i += n) {
+      uint32_t lo = 0u, hi = 0u;
+#pragma unroll
+      for (int l = 0; l < 4; ++l) {
+        lo |= ((i >> l) & 1u ? 0x1eu : 0u) << (8 * l);
+        hi |= ((i >> (l + 4)) & 1u ? 0x1eu : 0u) << (8 * l);
+      }
+      s3[i] = make_uint2(lo, hi);
+    }
+  }
+}
+
+template <int FMT>
+__device__ __forceinline__ IqTables iq_tables(const uint8_t* base) {
+  IqTables t{};
+  if (FMT == QG_FMT_IQ2S) {
+    t.kgrid2 = reinterpret_cast<const uint2*>(base);
+    t.sign2 = t.kgrid2 + 1024;
+  } else if (FMT == QG_FMT_IQ3S) {
+    t.grid3 = reinterpret_cast<const uint32_t*>(base);
+    t.sign3 = reinterpret_cast<const uint2*>(base + 2048);
+  }
+  return t;
+}
+
+constexpr uint32_t iq_table_bytes(int fmt) {
+  return fmt == QG_FMT_IQ2S ? 10240u : fmt == QG_FMT_IQ3S ? 4096u : 0u;
+}
+
+// A prepared activation: x quantized once (qg_act_prepare) into one 176-byte record
+// per 64-column chunk, the XChunk a GEMV thread would otherwise compute itself.
+struct __align__(16) ActChunk {
+  uint32_t ah[8], al[8], bh[8], bl[8];
+  float sa, sb, suma, sumb;
+  int qh[4], ql[4];
+};
+static_assert(sizeof(ActChunk) == 176, "prepared activation record is 176 bytes");
+
+__device__ __forceinline__ void load_act_chunk(const ActChunk* __restrict__ src, XChunk& x) {
+  const uint4* p = reinterpret_cast<const uint4*>(src);
+  uint4 v[11];
+#pragma unroll
+  for (int i = 0; i < 11; ++i) v[i] = __ldg(p + i);
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    x.ah[4 * i] = v[i].x; x.ah[4 * i + 1] = v[i].y; x.ah[4 * i + 2] = v[i].z; x.ah[4 * i + 3] = v[i].w;
+    x.al[4 * i] = v[2 + i].x; x.al[4 * i + 1] = v[2 + i].y; x.al[4 * i + 2] = v[2 + i].z; x.al[4 * i + 3] = v[2 + i].w;
+    x.bh[4 * i] = v[4 + i].x; x.bh[4 * i + 1] = v[4 + i].y; x.bh[4 * i + 2] = v[4 + i].z; x.bh[4 * i + 3] = v[4 + i].w;
+    x.bl[4 * i] = v[6 + i].x; x.bl[4 * i + 1] = v[6 + i].y; x.bl[4 * i + 2] = v[6 + i].z; x.bl[4 * i + 3] = v[6 + i].w;
+  }
+  x.sa = __uint_as_float(v[8].x); x.sb = __uint_as_float(v[8].y);
+  x.suma = __uint_as_float(v[8].z); x.sumb = __uint_as_float(v[8].w);
+  x.qh[0] = v[9].x; x.qh[1] = v[9].y; x.qh[2] = v[9].z; x.qh[3] = v[9].w;
+  x.ql[0] = v[10].x; x.ql[1] = v[10].y; x.ql[2] = v[10].z; x.ql[3] = v[10].w;
+}
+
+__device__ __forceinline__ void store_act_chunk(const XChunk& x, ActChunk* dst) {
+  uint4* p = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    p[i] = make_uint4(x.ah[4 * i], x.ah[4 * i + 1], x.ah[4 * i + 2], x.ah[4 * i + 3]);
+    p[2 + i] = make_uint4(x.al[4 * i], x.al[4 * i + 1], x.al[4 * i + 2], x.al[4 * i + 3]);
+    p[4 + i] = make_uint4(x.bh[4 * i], x.bh[4 * i + 1], x.bh[4 * i + 2], x.bh[4 * i + 3]);
+    p[6 + i] = make_uint4(x.bl[4 * i], x.bl[4 * i + 1], x.bl[4 * i + 2], x.bl[4 * i + 3]);
+  }
+  p[8] = make_uint4(__float_as_uint(x.sa), __float_as_uint(x.sb), __float_as_uint(x.suma),
+                    __float_as_uint(x.sumb));
+  p[9] = make_uint4(x.qh[0], x.qh[1], x.qh[2], x.qh[3]);
+  p[10] = make_uint4(x.ql[0], x.ql[1], x.ql[2], x.ql[3]);
+}
+
+// This thread's 64 columns of x, quantized to the two byte planes.
+__device__ __forceinline__ void load_x_chunk(const float* __restrict__ xp, bool vec, XChunk& x) {
+  float va[32], vb[32];
+  if (vec) {
+    const float4* x4 = reinterpret_cast<const float4*>(xp);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float4 a = __ldg(x4 + i), b = __ldg(x4 + 8 + i);
+      va[4 * i] = a.x; va[4 * i + 1] = a.y; va[4 * i + 2] = a.z; va[4 * i + 3] = a.w;
+      vb[4 * i] = b.x; vb[4 * i + 1] = b.y; vb[4 * i + 2] = b.z; vb[4 * i + 3] = b.w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      va[i] = __ldg(xp + i);
+      vb[i] = __ldg(xp + 32 + i);
+    }
+  }
+  quantize_half(va, x.ah, x.al, x.sa, x.suma, x.qh[0], x.ql[0], x.qh[1], x.ql[1]);
+  quantize_half(vb, x.bh, x.bl, x.sb, x.sumb, x.qh[2], x.ql[2], x.qh[3], x.ql[3]);
 }
 
 }  // namespace qg

@@ -1,23 +1,30 @@
 // qg_gemv.cu -- batch-1 quantized GEMV for sm_100a (the decode hot path).
 //
-// Design (one kernel per pack format, template FMT):
-//  * Persistent CTAs (grid = min(tiles, SMs x resident CTAs)).  A tile is a run of
-//    consecutive rows; its bytes are contiguous in the pack (payload and, for
-//    Q4_K split packs, metadata), so one elected thread streams each tile into a
-//    shared-memory ring of S stages with 1-D TMA (cp.async.bulk, mbarrier
-//    completion, L2 evict-first) while the other threads decode the previous ones.
-//  * Thread (slot, c) owns the 64-column chunk c of one row of every pass; it
-//    loads x[64c .. 64c+64) into registers once, so x is never re-read from
-//    memory, and each thread reads only the 32-48 B of its chunk from shared
-//    memory per row.
-//  * Row sums: shuffle reduction inside aligned lane groups of gcd(cols/64, 32),
-//    then one shared-memory pass per tile; the epilogue writes y (+ residual) and
-//    the reference's KV page word.
-//  * Every mbarrier wait is bounded (QG_ERR_WAIT_TIMEOUT); tiles whose byte count
-//    or address cannot go through TMA are copied by all threads instead.
+// Production kernel (gemv_tiled_kernel<FMT>), one instantiation per pack format:
+//  * Persistent CTAs, grid = min(tiles, SMs x resident CTAs).  A tile is a run of
+//    rpp x P consecutive rows, whose payload (and Q4_K split metadata) bytes are
+//    contiguous in the pack.  A dedicated producer warp streams the tile, a stage of
+//    rpp x Q rows at a time, into a ring of S shared-memory stages with 1-D TMA
+//    (cp.async.bulk, mbarrier completion, L2 evict-first); consumer warps release a
+//    stage with one mbarrier arrive per warp, so the pipeline never needs a CTA
+//    barrier.
+//  * Consumer thread (slot, c) owns the 64-column chunk c: its x values are loaded
+//    once, as two int8 planes, and every row's chunk is a string of dp4a
+//    instructions (qg_formats.cuh).  Row sums: shuffle reduction in lane groups of
+//    gcd(cols/64, 32), shared-memory partials, one consumer barrier per tile, then
+//    the epilogue (y, optional residual, the reference's KV page word).
+//  * Every mbarrier wait is bounded (QG_ERR_WAIT_TIMEOUT); the producer waits for its
+//    copies in flight before it exits.
+// gemv_staged_kernel<FMT> handles packs whose base address is not 16-B aligned
+// (all threads copy each tile); gemv_rowwise_kernel<FMT> decodes value by value for
+// rows wider than 32768 columns.
 #include <algorithm>
 #include <cstdio>
+#include <map>
 #include <mutex>
+#include <tuple>
+#include <set>
+#include <utility>
 
 #include "iq_grids.h"
 #include "qg_formats.cuh"
@@ -55,6 +62,11 @@ struct GemvArgs {
   uint32_t table_off;     // codebook offset in dynamic smem
   uint32_t stage_off;     // first stage offset in dynamic smem
   uint32_t tma_ok;        // base pointers 16-B aligned and full tiles 16-B multiples
+  uint32_t stage_rows;    // rows per pipeline stage (tiled kernel)
+  uint32_t stage_mask;    // passes per stage - 1 (a power of two)
+  uint32_t stage_shift;   // log2(passes per stage)
+  uint32_t x_vec;         // x is 16-B aligned (vector loads)
+  const ActChunk* xq;     // prepared activation (qg_act_prepare), or null: quantize x here
 };
 
 template <int FMT>
@@ -86,15 +98,13 @@ __device__ __forceinline__ bool tile_via_tma(const GemvArgs& a, uint32_t tile) {
 }
 
 template <int FMT>
-__global__ void __launch_bounds__(512, 1) gemv_kernel(const GemvArgs a) {
+__global__ void __launch_bounds__(512, 1) gemv_staged_kernel(const GemvArgs a) {
   constexpr uint32_t PB = FmtTraits<FMT>::payload_bytes;
   constexpr uint32_t MB = FmtTraits<FMT>::meta_bytes;
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
   float* red = reinterpret_cast<float*>(smem + a.red_off);
   uint8_t* stages = smem + a.stage_off;
-  uint16_t* kgrid = reinterpret_cast<uint16_t*>(smem + a.table_off);
-  uint32_t* grid3 = reinterpret_cast<uint32_t*>(smem + a.table_off);
 
   const uint32_t tid = threadIdx.x;
   const uint32_t nthreads = blockDim.x;
@@ -125,29 +135,13 @@ __global__ void __launch_bounds__(512, 1) gemv_kernel(const GemvArgs a) {
   }
 
   // Codebooks into shared memory (overlaps the first TMA loads).
-  if (FMT == QG_FMT_IQ2S) {
-    for (uint32_t i = tid; i < 1024u; i += nthreads) kgrid[i] = g_iq2s_kgrid[i];
-  } else if (FMT == QG_FMT_IQ3S) {
-    for (uint32_t i = tid; i < 512u; i += nthreads) grid3[i] = g_iq3s_grid[i];
-  }
-
-  // This thread's 64 x values and their two 32-value sums.
-  ChunkX xr;
-  {
-    const float* xp = a.x + 64u * c;
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      xr.a[i] = make_float2(__ldg(xp + 2 * i), __ldg(xp + 2 * i + 1));
-      xr.b[i] = make_float2(__ldg(xp + 32 + 2 * i), __ldg(xp + 33 + 2 * i));
-    }
-    float sa = 0.f, sb = 0.f;
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      sa += xr.a[i].x + xr.a[i].y;
-      sb += xr.b[i].x + xr.b[i].y;
-    }
-    xr.sa = sa;
-    xr.sb = sb;
+  build_iq_tables<FMT>(smem + a.table_off, tid, nthreads);
+  const IqTables tables = iq_tables<FMT>(smem + a.table_off);
+  XChunk xr;
+  if (a.xq != nullptr) {
+    load_act_chunk(a.xq + c, xr);
+  } else {
+    load_x_chunk(a.x + 64u * c, a.x_vec != 0u, xr);
   }
   const uint32_t tok = (a.kv != nullptr && a.token != nullptr) ? *a.token : 0u;
   __syncthreads();  // codebooks visible
@@ -185,7 +179,7 @@ __global__ void __launch_bounds__(512, 1) gemv_kernel(const GemvArgs a) {
       if (valid && lr < nrows) {
         const uint8_t* rp = st + static_cast<uint64_t>(lr) * bpr * PB;
         const uint8_t* rm = st + a.meta_off + static_cast<uint64_t>(lr) * bpr * MB;
-        part = chunk_dot<FMT>(rp, rm, c, xr, kgrid, grid3);
+        part = chunk_dot<FMT>(rp, rm, c, xr, tables);
       }
       for (uint32_t off = a.group >> 1; off > 0u; off >>= 1) {
         part += __shfl_xor_sync(0xffffffffu, part, off);
@@ -255,6 +249,174 @@ __global__ void __launch_bounds__(256) gemv_rowwise_kernel(const GemvArgs a) {
 }
 
 // ---------------------------------------------------------------------------
+// Tiled kernel: the production path for 16-B aligned packs.
+
+// Issue the TMA for stage `s` holding rows [row_begin, row_begin + stage_rows) of the
+// pack (fewer at its end).  The last stage of a pack may end off a 16-B boundary:
+// its tail bytes are copied here, before the arrive that publishes the stage.
+template <int FMT>
+__device__ __forceinline__ void tiled_issue(const GemvArgs& a, uint8_t* st, uint64_t* bar,
+                                            uint32_t row_begin, uint64_t policy) {
+  constexpr uint32_t PB = FmtTraits<FMT>::payload_bytes;
+  constexpr uint32_t MB = FmtTraits<FMT>::meta_bytes;
+  const uint32_t bpr = a.cols >> 8;
+  uint32_t nr = 0u;
+  if (row_begin < a.rows) nr = min(a.stage_rows, a.rows - row_begin);
+  const uint32_t pb = nr * bpr * PB, mb = nr * bpr * MB;
+  const uint32_t pb16 = pb & ~15u, mb16 = mb & ~15u;
+  const uint8_t* src = a.payload + static_cast<uint64_t>(row_begin) * bpr * PB;
+  const uint8_t* msrc = a.meta + static_cast<uint64_t>(row_begin) * bpr * MB;
+  for (uint32_t o = pb16; o < pb; ++o) st[o] = src[o];
+  if (MB != 0u) {
+    for (uint32_t o = mb16; o < mb; ++o) st[a.meta_off + o] = msrc[o];
+  }
+  mbar_arrive_expect_tx(bar, pb16 + mb16);
+  if (pb16 != 0u) tma_load_1d(st, src, pb16, bar, policy);
+  if (MB != 0u && mb16 != 0u) tma_load_1d(st + a.meta_off, msrc, mb16, bar, policy);
+}
+
+__device__ __forceinline__ void consumer_sync(uint32_t nconsumers) {
+  asm volatile("bar.sync 1, %0;" ::"r"(nconsumers) : "memory");
+}
+
+// Sum over an aligned lane group of `group` lanes (4, 8, 16 or 32; warp-uniform).
+__device__ __forceinline__ float group_sum(float v, uint32_t group) {
+  if (group > 16u) v += __shfl_xor_sync(0xffffffffu, v, 16);
+  if (group > 8u) v += __shfl_xor_sync(0xffffffffu, v, 8);
+  if (group > 4u) v += __shfl_xor_sync(0xffffffffu, v, 4);
+  v += __shfl_xor_sync(0xffffffffu, v, 2);
+  v += __shfl_xor_sync(0xffffffffu, v, 1);
+  return v;
+}
+
+template <int FMT>
+__global__ void __launch_bounds__(544, 1) gemv_tiled_kernel(const GemvArgs a) {
+  constexpr uint32_t PB = FmtTraits<FMT>::payload_bytes;
+  constexpr uint32_t MB = FmtTraits<FMT>::meta_bytes;
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* empty = full + 8;
+  float* red = reinterpret_cast<float*>(smem + a.red_off);
+  uint8_t* stages = smem + a.stage_off;
+
+  const uint32_t tid = threadIdx.x, lane = tid & 31u;
+  const uint32_t nconsumers = blockDim.x - 32u;  // the last warp is the producer
+  const uint32_t first = blockIdx.x, stride = gridDim.x;
+  const uint32_t n_my = a.num_tiles > first ? (a.num_tiles - first + stride - 1u) / stride : 0u;
+  const uint32_t loads_per_tile = a.passes >> a.stage_shift;
+  const uint32_t S = a.stages;
+
+  if (tid == 0u) {
+    for (uint32_t s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1u);
+      mbar_init(&empty[s], nconsumers >> 5);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (tid >= nconsumers) {
+    // Producer warp: one elected lane streams every stage of this CTA's tiles.
+    if (lane == 0u) {
+      const uint64_t policy = l2_evict_first_policy();
+      bool ok = true;
+      uint32_t s = 0, ephase = 0, issued = 0;
+      for (uint32_t i = 0; i < n_my && ok; ++i) {
+        const uint32_t row0 = (first + i * stride) * a.rows_per_tile;
+        for (uint32_t j = 0; j < loads_per_tile; ++j) {
+          if (issued >= S) {
+            ok = mbar_wait_bounded(&empty[s], ephase);
+            if (!ok) break;
+          }
+          tiled_issue<FMT>(a, stages + s * a.stage_bytes, &full[s], row0 + j * a.stage_rows, policy);
+          ++issued;
+          if (++s == S) {
+            s = 0;
+            if (issued > S) ephase ^= 1u;
+          }
+        }
+      }
+      // Copies still in flight must land before this CTA's shared memory is released:
+      // wait for the last min(S, issued) stages (bounded).
+      if (ok) {
+        const uint32_t n = min(S, issued);
+        for (uint32_t k = 0; k < n; ++k) {
+          const uint32_t L = issued - n + k;
+          mbar_wait_bounded(&full[L % S], (L / S) & 1u);
+        }
+      }
+    }
+    return;
+  }
+
+  const bool valid = tid < a.rpp * a.tpr;
+  const uint32_t slot = valid ? tid / a.tpr : 0u;
+  const uint32_t c = valid ? tid - slot * a.tpr : 0u;
+  const uint32_t bpr = a.cols >> 8;
+  const uint32_t gpr = a.tpr / a.group;
+  const uint32_t gidx = c / a.group;
+  const bool leader = valid && (c & (a.group - 1u)) == 0u;
+  const uint32_t row_stride = bpr * PB, meta_stride = bpr * MB;
+  const uint32_t Q = a.stage_rows / a.rpp;
+
+  build_iq_tables<FMT>(smem + a.table_off, tid, nconsumers);
+  const IqTables tables = iq_tables<FMT>(smem + a.table_off);
+  XChunk xr;
+  if (a.xq != nullptr) {
+    load_act_chunk(a.xq + c, xr);
+  } else {
+    load_x_chunk(a.x + 64u * c, a.x_vec != 0u, xr);
+  }
+  const uint32_t tok = (a.kv != nullptr && a.token != nullptr) ? *a.token : 0u;
+  consumer_sync(nconsumers);  // tables visible
+
+  uint32_t s = 0, phase = 0;
+  bool failed = false;
+  for (uint32_t i = 0; i < n_my && !failed; ++i) {
+    const uint32_t row0 = (first + i * stride) * a.rows_per_tile;
+    const uint32_t nrows = min(a.rows_per_tile, a.rows - row0);
+    float* rb = red + (i & 1u) * (a.rows_per_tile * gpr);
+    for (uint32_t j = 0; j < loads_per_tile; ++j) {
+      if (!mbar_wait_bounded(&full[s], phase)) failed = true;
+      const uint8_t* st = stages + s * a.stage_bytes;
+      const uint32_t lr0 = j * a.stage_rows + slot;  // tile row of q = 0
+#pragma unroll 2
+      for (uint32_t q = 0; q < Q; ++q) {
+        const uint32_t lr = lr0 + q * a.rpp;
+        const bool live = valid && lr < nrows && !failed;
+        float part = 0.f;
+        if (live) {
+          const uint32_t ls = q * a.rpp + slot;
+          part = chunk_dot<FMT>(st + ls * row_stride, st + a.meta_off + ls * meta_stride, c, xr,
+                                tables);
+        }
+        part = group_sum(part, a.group);
+        if (leader && live) rb[lr * gpr + gidx] = part;
+      }
+      __syncwarp();
+      if (lane == 0u) mbar_arrive(&empty[s]);
+      if (++s == S) {
+        s = 0;
+        phase ^= 1u;
+      }
+    }
+    consumer_sync(nconsumers);
+    for (uint32_t t = tid; t < nrows; t += nconsumers) {
+      float v = 0.f;
+      for (uint32_t g = 0; g < gpr; ++g) v += rb[t * gpr + g];
+      const uint32_t row = row0 + t;
+      if (a.residual != nullptr) v += a.residual[row];
+      a.y[row] = v;
+      if (a.kv != nullptr && row < a.active_pages && a.kv_words > 0u && a.page_words > 0u) {
+        const uint64_t kb = static_cast<uint64_t>(row) * a.page_words;
+        const uint64_t ko = (tok + row) % a.page_words;
+        a.kv[(kb + ko) % a.kv_words] = v;
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Host-side planning and launch.
 
 namespace {
@@ -287,22 +449,46 @@ DeviceInfo device_info() {
   return cache[dev];
 }
 
-template <int FMT>
-cudaError_t launch_gemv_fmt(GemvArgs a, cudaStream_t stream) {
-  constexpr uint32_t PB = FmtTraits<FMT>::payload_bytes;
-  constexpr uint32_t MB = FmtTraits<FMT>::meta_bytes;
-  const DeviceInfo dev = device_info();
-  const uint32_t bpr = a.cols >> 8;
-  a.tpr = a.cols / 64u;
-  if (a.cols < 256u || a.tpr > 512u) {
-    gemv_rowwise_kernel<FMT><<<a.rows, 256, 0, stream>>>(a);
-    return cudaGetLastError();
+template <typename K>
+cudaError_t ensure_smem_attr(K kernel, int max_optin) {
+  // One attribute set per (kernel, device); cudaFuncSetAttribute is cheap but not free.
+  static std::mutex mu;
+  static std::set<std::pair<const void*, int>> done;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const auto key = std::make_pair(reinterpret_cast<const void*>(kernel), dev);
+  std::lock_guard<std::mutex> lock(mu);
+  if (done.count(key) == 0u) {
+    const cudaError_t e =
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, max_optin);
+    if (e != cudaSuccess) return e;
+    done.insert(key);
   }
-  GemvPlan plan = plan_gemv(FMT, a.rows, a.cols, dev.sms);
-  if (plan.smem_bytes > static_cast<uint32_t>(dev.max_smem_optin)) {
-    gemv_rowwise_kernel<FMT><<<a.rows, 256, 0, stream>>>(a);
-    return cudaGetLastError();
+  return cudaSuccess;
+}
+
+// Resident CTAs per SM for a kernel at a block size and dynamic smem (cached).
+template <typename K>
+uint32_t resident_ctas(K kernel, uint32_t threads, uint32_t smem) {
+  static std::mutex mu;
+  static std::map<std::tuple<const void*, uint32_t, uint32_t, int>, uint32_t> cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const auto key = std::make_tuple(reinterpret_cast<const void*>(kernel), threads, smem, dev);
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  int n = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, static_cast<int>(threads), smem) !=
+          cudaSuccess ||
+      n < 1) {
+    n = 1;
   }
+  cache[key] = static_cast<uint32_t>(n);
+  return static_cast<uint32_t>(n);
+}
+
+void fill_args(GemvArgs& a, const GemvPlan& plan) {
   a.group = plan.group;
   a.rpp = plan.rpp;
   a.passes = plan.passes;
@@ -314,86 +500,157 @@ cudaError_t launch_gemv_fmt(GemvArgs a, cudaStream_t stream) {
   a.red_off = plan.red_off;
   a.table_off = plan.table_off;
   a.stage_off = plan.stage_off;
+  a.stage_rows = plan.stage_rows;
+  a.stage_mask = plan.stage_passes - 1u;
+  a.stage_shift = static_cast<uint32_t>(__builtin_ctz(plan.stage_passes));
+}
+
+template <int FMT>
+cudaError_t launch_gemv_fmt(GemvArgs a, cudaStream_t stream) {
+  constexpr uint32_t MB = FmtTraits<FMT>::meta_bytes;
+  const DeviceInfo dev = device_info();
+  a.tpr = a.cols / 64u;
+  a.x_vec = (reinterpret_cast<uintptr_t>(a.x) & 15u) == 0u ? 1u : 0u;
+  if (a.cols < 256u || a.tpr > 512u) {
+    gemv_rowwise_kernel<FMT><<<a.rows, 256, 0, stream>>>(a);
+    return cudaGetLastError();
+  }
   const bool aligned = (reinterpret_cast<uintptr_t>(a.payload) & 15u) == 0u &&
                        (MB == 0u || (reinterpret_cast<uintptr_t>(a.meta) & 15u) == 0u);
-  a.tma_ok = (aligned && ((a.rows_per_tile * bpr * PB) & 15u) == 0u &&
-              ((a.rows_per_tile * bpr * MB) & 15u) == 0u)
-                 ? 1u
-                 : 0u;
-  const size_t smem = plan.smem_bytes;
-  static thread_local int configured[64][QG_FMT_COUNT] = {};
-  int devid = 0;
-  cudaGetDevice(&devid);
-  if (devid >= 0 && devid < 64 && configured[devid][FMT] < static_cast<int>(smem)) {
-    cudaError_t e = cudaFuncSetAttribute(gemv_kernel<FMT>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         dev.max_smem_optin);
-    if (e != cudaSuccess) return e;
-    configured[devid][FMT] = dev.max_smem_optin;
+  if (aligned) {
+    const GemvPlan plan = plan_gemv(FMT, a.rows, a.cols, dev.sms);
+    if (plan.tiled && plan.smem_bytes <= static_cast<uint32_t>(dev.max_smem_optin)) {
+      fill_args(a, plan);
+      a.tma_ok = 1u;
+      const cudaError_t e = ensure_smem_attr(gemv_tiled_kernel<FMT>, dev.max_smem_optin);
+      if (e != cudaSuccess) return e;
+      const uint32_t per_sm = resident_ctas(gemv_tiled_kernel<FMT>, plan.threads, plan.smem_bytes);
+      const uint32_t grid = std::max(1u, std::min(plan.num_tiles, per_sm * dev.sms));
+      gemv_tiled_kernel<FMT><<<grid, plan.threads, plan.smem_bytes, stream>>>(a);
+      return cudaGetLastError();
+    }
   }
-  gemv_kernel<FMT><<<plan.grid, plan.threads, smem, stream>>>(a);
+  // Unaligned packs (or shapes the tiled plan cannot stage): all-thread copies.
+  const GemvPlan plan = plan_staged(FMT, a.rows, a.cols, dev.sms);
+  if (plan.smem_bytes > static_cast<uint32_t>(dev.max_smem_optin)) {
+    gemv_rowwise_kernel<FMT><<<a.rows, 256, 0, stream>>>(a);
+    return cudaGetLastError();
+  }
+  fill_args(a, plan);
+  a.tma_ok = 0u;
+  const cudaError_t e = ensure_smem_attr(gemv_staged_kernel<FMT>, dev.max_smem_optin);
+  if (e != cudaSuccess) return e;
+  const uint32_t per_sm = resident_ctas(gemv_staged_kernel<FMT>, plan.threads, plan.smem_bytes);
+  const uint32_t grid = std::max(1u, std::min(plan.num_tiles, per_sm * dev.sms));
+  gemv_staged_kernel<FMT><<<grid, plan.threads, plan.smem_bytes, stream>>>(a);
   return cudaGetLastError();
+}
+
+// Threads per CTA: rows-per-pass is the smallest multiple of 32/group (whole warps)
+// that reaches ~256 threads; rows wider than 512 threads pad the last warp.
+void plan_threads(uint32_t tpr, GemvPlan& p) {
+  p.group = gcd_u32(tpr, 32u);
+  const uint32_t base = 32u / p.group;
+  uint32_t rpp = base;
+  if (rpp * tpr > 512u) rpp = 1u;
+  while ((rpp + base) * tpr <= 256u) rpp += base;
+  p.rpp = rpp;
+  p.threads = ((rpp * tpr + 31u) / 32u) * 32u;
+}
+
+void plan_smem(int fmt, uint32_t tpr, GemvPlan& p) {
+  const uint32_t red_floats = 2u * p.rows_per_tile * (tpr / p.group);
+  p.red_off = 256u;  // 16 mbarriers
+  p.table_off = (p.red_off + red_floats * 4u + 127u) & ~127u;
+  const uint32_t table_bytes = iq_table_bytes(fmt);
+  p.stage_off = (p.table_off + table_bytes + 127u) & ~127u;
+  p.smem_bytes = p.stage_off + p.stages * p.stage_bytes;
+}
+
+uint32_t ctas_per_sm(const GemvPlan& p) {
+  const uint32_t by_smem = std::max(1u, (228u * 1024u) / (p.smem_bytes + 1024u));
+  const uint32_t by_threads = std::max(1u, 2048u / p.threads);
+  const uint32_t by_regs = std::max(1u, 65536u / (p.threads * 128u));
+  return std::min(by_smem, std::min(by_threads, by_regs));
 }
 
 }  // namespace
 
+// Plan of the tiled kernel.  passes P in {32, 16, 8, 4}: the largest that still gives
+// every resident CTA at least two tiles; stage = Q passes (Q | P) of ~16 KB whose
+// byte count is a multiple of 16; S stages within ~96 KB (2..8).
 GemvPlan plan_gemv(int fmt, uint32_t rows, uint32_t cols, int sms) {
   GemvPlan p{};
   const uint32_t PB = qg_payload_bytes_per_block(fmt);
   const uint32_t MB = qg_meta_bytes_per_block(fmt);
-  const uint32_t bpr = cols >> 8;
-  const uint32_t tpr = cols / 64u;
-  p.group = gcd_u32(tpr, 32u);
-  // Smallest rows-per-pass whose thread count is a whole number of warps, then as
-  // many as fit in ~256 threads.
-  const uint32_t base = 32u / p.group;
-  uint32_t rpp = base;
-  if (rpp * tpr > 512u) rpp = 1u;  // pad the last warp with idle threads
-  while ((rpp + base) * tpr <= 256u) rpp += base;
-  p.rpp = rpp;
-  p.threads = ((rpp * tpr + 31u) / 32u) * 32u;
+  const uint32_t bpr = cols >> 8, tpr = cols / 64u;
+  plan_threads(tpr, p);
   const uint32_t row_bytes = bpr * PB, row_meta = bpr * MB;
-  // ~16 KB of payload per tile, at most 4 passes.
-  uint32_t passes = std::max(1u, std::min(4u, 16384u / std::max(1u, rpp * row_bytes)));
-  // Full tiles must be 16-B multiples to go through TMA.
-  for (uint32_t k = passes; k <= passes * 16u; ++k) {
-    if (((k * rpp * row_bytes) & 15u) == 0u && ((k * rpp * row_meta) & 15u) == 0u) {
-      passes = k;
-      break;
-    }
+  // Stage: smallest power-of-two passes with 16-B aligned bytes, grown toward 16 KB.
+  uint32_t q = 1u;
+  while (q <= 32u && (((q * p.rpp * row_bytes) & 15u) != 0u || ((q * p.rpp * row_meta) & 15u) != 0u)) {
+    q <<= 1;
   }
+  if (q > 32u) {
+    p.tiled = 0u;
+    return p;
+  }
+  const uint32_t q_align = q;
+  while (q < 16u && 2u * q * p.rpp * (row_bytes + row_meta) <= 16384u) q <<= 1;
+  const uint32_t resident = static_cast<uint32_t>(sms) * 2u;
+  uint32_t P = 32u;
+  while (P > 4u && (rows + P * p.rpp - 1u) / (P * p.rpp) < 2u * resident) P >>= 1;
+  P = std::max(P, q_align);  // a stage is never smaller than its aligned size
+  q = std::min(q, P);        // both powers of two >= q_align: q stays aligned
+  p.passes = P;
+  p.stage_passes = q;
+  p.stage_rows = q * p.rpp;
+  p.rows_per_tile = P * p.rpp;
+  p.num_tiles = (rows + p.rows_per_tile - 1u) / p.rows_per_tile;
+  const uint32_t pay = p.stage_rows * row_bytes, met = p.stage_rows * row_meta;
+  p.meta_off = (pay + 127u) & ~127u;
+  p.stage_bytes = MB ? ((p.meta_off + met + 127u) & ~127u) : ((pay + 127u) & ~127u);
+  p.stages = std::max(2u, std::min(8u, (96u * 1024u) / p.stage_bytes));
+  p.threads += 32u;  // producer warp
+  plan_smem(fmt, tpr, p);
+  p.grid = std::max(1u, std::min(p.num_tiles, static_cast<uint32_t>(sms) * ctas_per_sm(p)));
+  p.tiled = 1u;
+  return p;
+}
+
+// Plan of the all-thread-copy kernel (one row pass per thread per tile row group).
+GemvPlan plan_staged(int fmt, uint32_t rows, uint32_t cols, int sms) {
+  GemvPlan p{};
+  const uint32_t PB = qg_payload_bytes_per_block(fmt);
+  const uint32_t MB = qg_meta_bytes_per_block(fmt);
+  const uint32_t bpr = cols >> 8, tpr = cols / 64u;
+  plan_threads(tpr, p);
+  const uint32_t row_bytes = bpr * PB, row_meta = bpr * MB;
+  const uint32_t passes = std::max(1u, std::min(4u, 16384u / std::max(1u, p.rpp * row_bytes)));
   p.passes = passes;
-  p.rows_per_tile = passes * rpp;
+  p.stage_passes = 1u;
+  p.rows_per_tile = passes * p.rpp;
+  p.stage_rows = p.rows_per_tile;
   p.num_tiles = (rows + p.rows_per_tile - 1u) / p.rows_per_tile;
   const uint32_t pay = p.rows_per_tile * row_bytes, met = p.rows_per_tile * row_meta;
   p.meta_off = (pay + 127u) & ~127u;
-  p.stage_bytes = (p.meta_off + met + 127u) & ~127u;
-  if (MB == 0u) p.stage_bytes = (pay + 127u) & ~127u;
-  const uint32_t budget = 96u * 1024u;
-  p.stages = std::max(2u, std::min(8u, budget / p.stage_bytes));
-  const uint32_t red_floats = 2u * p.rows_per_tile * (tpr / p.group);
-  p.red_off = 128u;
-  p.table_off = (p.red_off + red_floats * 4u + 127u) & ~127u;
-  const uint32_t table_bytes = (fmt == QG_FMT_IQ2S || fmt == QG_FMT_IQ3S) ? 2048u : 0u;
-  p.stage_off = (p.table_off + table_bytes + 127u) & ~127u;
-  p.smem_bytes = p.stage_off + p.stages * p.stage_bytes;
-  const uint32_t by_smem = std::max(1u, (228u * 1024u) / (p.smem_bytes + 1024u));
-  const uint32_t by_threads = std::max(1u, 2048u / p.threads);
-  const uint32_t by_regs = std::max(1u, 65536u / (p.threads * 128u));
-  const uint32_t per_sm = std::min(by_smem, std::min(by_threads, by_regs));
-  p.grid = std::min(p.num_tiles, static_cast<uint32_t>(sms) * per_sm);
-  if (p.grid == 0u) p.grid = 1u;
+  p.stage_bytes = MB ? ((p.meta_off + met + 127u) & ~127u) : ((pay + 127u) & ~127u);
+  p.stages = std::max(2u, std::min(8u, (96u * 1024u) / p.stage_bytes));
+  plan_smem(fmt, tpr, p);
+  p.grid = std::max(1u, std::min(p.num_tiles, static_cast<uint32_t>(sms) * ctas_per_sm(p)));
+  p.tiled = 0u;
   return p;
 }
 
 cudaError_t launch_gemv(int fmt, const uint8_t* payload, const uint8_t* meta, const float* x,
-                        float* y, const float* residual, float* kv, const uint32_t* token,
-                        uint64_t kv_words, uint32_t page_words, uint32_t active_pages,
-                        uint32_t rows, uint32_t cols, cudaStream_t stream) {
+                        const void* act, float* y, const float* residual, float* kv,
+                        const uint32_t* token, uint64_t kv_words, uint32_t page_words,
+                        uint32_t active_pages, uint32_t rows, uint32_t cols, cudaStream_t stream) {
   GemvArgs a{};
   a.payload = payload;
   a.meta = meta;
   a.x = x;
+  a.xq = static_cast<const ActChunk*>(act);
   a.y = y;
   a.residual = residual;
   a.kv = kv;

@@ -12,16 +12,26 @@ namespace qg {
 struct GemvPlan {
   uint32_t grid, threads, group, rpp, passes, rows_per_tile, num_tiles, stages;
   uint32_t stage_bytes, meta_off, red_off, table_off, stage_off, smem_bytes;
+  uint32_t stage_passes, stage_rows, tiled;
 };
 
+// Tiled (TMA-pipelined) plan; .tiled == 0 when the shape cannot be staged that way.
 GemvPlan plan_gemv(int fmt, uint32_t rows, uint32_t cols, int sms);
+// Plan of the all-thread-copy kernel used for packs that are not 16-B aligned.
+GemvPlan plan_staged(int fmt, uint32_t rows, uint32_t cols, int sms);
 
 // y = W x (+ residual); optional reference KV page write with the token read on
 // the device before the launch's first row is stored.
+// `act` (optional) is x prepared by launch_act_prepare; the kernel then skips its own
+// quantization of x.
 cudaError_t launch_gemv(int fmt, const uint8_t* payload, const uint8_t* meta, const float* x,
-                        float* y, const float* residual, float* kv, const uint32_t* token,
-                        uint64_t kv_words, uint32_t page_words, uint32_t active_pages,
-                        uint32_t rows, uint32_t cols, cudaStream_t stream);
+                        const void* act, float* y, const float* residual, float* kv,
+                        const uint32_t* token, uint64_t kv_words, uint32_t page_words,
+                        uint32_t active_pages, uint32_t rows, uint32_t cols, cudaStream_t stream);
+
+// Bytes of a prepared activation of `cols` values (176 per 64 columns).
+inline size_t act_bytes(uint32_t cols) { return static_cast<size_t>(cols / 64u) * 176u; }
+cudaError_t launch_act_prepare(const float* x, uint32_t cols, void* act, cudaStream_t stream);
 
 // token = (argmax(v[0:n]) + offset + add_token * token) % modulus (one CTA).
 cudaError_t launch_argmax_token(const float* v, uint32_t n, uint32_t* token, uint32_t offset,

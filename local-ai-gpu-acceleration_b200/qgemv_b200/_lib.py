@@ -52,6 +52,9 @@ SIGNATURES: dict[str, list] = {
     "rtxllm_launch_rmsnorm_cache": [P, P, U32, U32, c_float, U32, P],
     "rtxllm_launch_rmsnorm_cache_and_gated_product": [P, P, P, P, U32, U32, U32, c_float, U32, P],
     "qg_gemv": [c_int, P, P, P, P, U32, U32, P],
+    "qg_act_bytes": [U32, P],
+    "qg_act_prepare": [P, U32, P, P],
+    "qg_gemv_act": [c_int, P, P, P, P, P, U32, U32, P],
     "qg_decode_stage": [c_int, P, P, P, P, P, P, U32, U32, U32, U32, U32, P],
     "qg_gemv_batched": [c_int, P, P, P, P, U32, U32, U32, P],
     "qg_dequantize": [c_int, P, P, U64, U64, P, P],

@@ -40,6 +40,33 @@ def gemv(fmt: int, payload: torch.Tensor, meta: torch.Tensor | None, x: torch.Te
     return y
 
 
+def act_bytes(cols: int) -> int:
+    import ctypes
+
+    n = ctypes.c_size_t(0)
+    check("qg_act_bytes", cols, ctypes.addressof(n))
+    return n.value
+
+
+def act_prepare(x: torch.Tensor, act: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    require_cuda()
+    cols = x.numel()
+    if act is None:
+        act = torch.empty(act_bytes(cols), dtype=torch.uint8, device=x.device)
+    check("qg_act_prepare", _ptr(x), cols, _ptr(act), _stream(stream))
+    return act
+
+
+def gemv_act(fmt: int, payload, meta, x: torch.Tensor, act: torch.Tensor, rows: int, cols: int,
+             y: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    require_cuda()
+    if y is None:
+        y = torch.empty(rows, dtype=torch.float32, device=x.device)
+    check("qg_gemv_act", fmt, _ptr(payload), _ptr(meta), _ptr(x), _ptr(act), _ptr(y), rows, cols,
+          _stream(stream))
+    return y
+
+
 def gemv_batched(fmt: int, payload, meta, x: torch.Tensor, rows: int, cols: int,
                  y: torch.Tensor | None = None, stream=None) -> torch.Tensor:
     require_cuda()

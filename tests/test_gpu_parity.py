@@ -276,3 +276,31 @@ def test_batched_vs_oracle(cuda, port):
 def test_error_word_is_clear(cuda):
     torch.cuda.synchronize()
     assert ops.get_error() == 0
+
+
+@pytest.mark.parametrize("fmt", list(FORMAT_TAGS))
+@pytest.mark.parametrize("rows,cols", [(37, 1792), (300, 4096), (64, 14336)])
+def test_prepared_activation_gemv_vs_oracle(cuda, port, fmt, rows, cols):
+    """qg_act_prepare once, then qg_gemv_act: same tolerance as qg_gemv."""
+    pk = packs.synthetic_pack(fmt, rows, cols, seed=rows + 7 * cols + fmt)
+    x = packs.synthetic_activation(cols, fmt + 3)
+    xd = dev(x, cuda)
+    act = ops.act_prepare(xd)
+    y = ops.gemv_act(fmt, dev(pk.payload, cuda), dev(pk.meta, cuda), xd, act, rows, cols)
+    want = port.matvec(fmt, pk.payload, pk.meta, x, rows, cols)
+    assert_rows_close(y.cpu().numpy(), want, row_tol(port, fmt, pk.payload, pk.meta, x, rows, cols))
+    y2 = ops.gemv(fmt, dev(pk.payload, cuda), dev(pk.meta, cuda), xd, rows, cols)
+    assert torch.equal(y, y2)  # same planes, same arithmetic
+
+
+def test_activation_extremes(cuda, port):
+    """x with zeros, one huge value and tiny values: the per-32-column scale handles it."""
+    rows, cols = 40, 2048
+    pk = packs.synthetic_pack(packs.Q4K_RAW, rows, cols, seed=3)
+    x = packs.synthetic_activation(cols, 3)
+    x[:64] = 0.0
+    x[100] = 3.0e4
+    x[200:260] *= 1e-6
+    y = ops.gemv(packs.Q4K_RAW, dev(pk.payload, cuda), None, dev(x, cuda), rows, cols)
+    want = port.matvec(packs.Q4K_RAW, pk.payload, None, x, rows, cols)
+    assert_rows_close(y.cpu().numpy(), want, row_tol(port, packs.Q4K_RAW, pk.payload, None, x, rows, cols))

@@ -166,3 +166,17 @@ def test_port_matches_live_reference(port, fmt):
     b = ref.matvec(fmt, pk.payload, pk.meta, x, 19, 1280)
     assert same_bits(a, b)
     assert same_bits(port.dequant(fmt, pk.payload, pk.meta, 3, 5), ref.dequant(fmt, pk.payload, pk.meta, 3, 5))
+
+
+def test_codebook_properties_used_by_the_kernels():
+    """The GEMV turns IQ3_S magnitudes g into g XOR 0x11 / g XOR 0x0F (= 15 +- g): every
+    grid byte must be odd and <= 15; IQ2_S codes are 2-bit by construction."""
+    sys.path.insert(0, str(REPO / "oracle"))
+    import gen_iq_grids
+
+    iq2s, iq3s = gen_iq_grids.parse_header(gen_iq_grids.DEFAULT_OUT)
+    assert len(iq2s) == 1024 and all(0 <= v < 65536 for v in iq2s)
+    for v in iq3s:
+        for k in range(4):
+            b = (v >> (8 * k)) & 0xFF
+            assert b % 2 == 1 and b <= 15
