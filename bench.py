@@ -175,6 +175,38 @@ def run_reference(args) -> int:
     return 0
 
 
+def measure_slice(device, args) -> dict:
+    """one mixed-format layer slice (hidden 4096, Q/K/V/O IQ3_S,
+    gate/up IQ2_S, down Q5_K) captured as one graph with the C-ABI graph API and
+    replayed; reported beside the headline metric."""
+    import torch
+
+    from qgemv_b200.slice import LayerSlice, StepGraph
+
+    sl = LayerSlice(seed=3, device=device)
+    x = torch.randn(sl.dims["hidden"], device=device)
+    out = torch.empty_like(x)
+    stream = torch.cuda.Stream(device)
+    sl.forward(x, out, stream)  # eager warm-up (kernel attributes)
+    stream.synchronize()
+    g = StepGraph(stream, lambda: sl.forward(x, out, stream))
+    for _ in range(max(3, args.warmup)):
+        g.launch()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    n = max(20, args.steps * 5)
+    e0.record(stream)
+    for _ in range(n):
+        g.launch()
+    e1.record(stream)
+    stream.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / n
+    g.close()
+    return {"workload": "BASELINE config 3 layer slice, 8 kernels in one graph",
+            "us_per_step": us, "steps_per_s": 1e6 / us,
+            "weight_bytes": sl.weight_bytes, "GBps": sl.weight_bytes / (us * 1e-6) / 1e9}
+
+
 def run_ours(args) -> int:
     import torch
     import torch.distributed as dist
@@ -322,6 +354,7 @@ def run_ours(args) -> int:
     e2e_value = world * bytes_per_step * args.steps / (e2e_ms * 1e-3) / 1e9
     del graphs, step_graph
 
+    slice_stats = measure_slice(device, args)
     err = ops.get_error()
     if rank == 0:
         cpu = cpu_reference_sample(8, os.cpu_count() or 1) if world == 1 and not args.only else None
@@ -340,6 +373,7 @@ def run_ours(args) -> int:
             "clocks": clocks.summary(),
             "error_word": err,
             "per_matvec": per,
+            "slice": slice_stats,
         }
         print(json.dumps(line))
     if world > 1:

@@ -16,10 +16,11 @@
  *     error word.  They have no counterpart in the reference unless a citation
  *     says so.
  *
- * Every pointer is caller-owned device memory unless stated otherwise.  No entry
- * point allocates, synchronizes or touches host memory (qg_get_error excepted), so
- * all of them can be recorded into a CUDA graph.  Errors: invalid arguments return
- * cudaErrorInvalidValue before any launch; otherwise the result of
+ * Every pointer is caller-owned device memory unless stated otherwise.  No launching
+ * entry point allocates, synchronizes or touches host memory, so all of them can be
+ * recorded into a CUDA graph; the exceptions are qg_get_error (reads the error word)
+ * and the qg_graph_* functions (they build and own a graph).  Errors: invalid
+ * arguments return cudaErrorInvalidValue before any launch; otherwise the result of
  * cudaGetLastError() after the launches.
  */
 #ifndef QGEMV_B200_H_
@@ -257,6 +258,56 @@ cudaError_t qg_dequantize(int fmt, const uint8_t* payload, const uint8_t* meta,
 cudaError_t qg_argmax_token(const float* values, uint32_t n, uint32_t* token,
                             uint32_t token_offset, uint32_t add_token, uint32_t modulus,
                             cudaStream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Mixed-format layer slice (no reference counterpart for the
+ * weighted RMSNorm, the SiLU gate or the residual add -- the reference's slice uses
+ * unweighted feedback kernels and a passthrough attention phase,
+ * runtime/apps/mixed_sequence_benchmark_runner/main.cpp:195,4073-4280):
+ *   h = x / sqrt(mean(x^2) + eps) * norm_weight
+ *   q = Wq h,  k = Wk h,  v = Wv h           (attn_fmt; Wq [q_rows x hidden],
+ *                                              Wk/Wv [kv_rows x hidden])
+ *   o = Wo q                                 (attention passthrough; Wo [hidden x q_rows])
+ *   a = silu(Wg o) * (Wu o)                  (ffn_fmt; Wg/Wu [ffn x hidden])
+ *   out = x + Wd a                           (down_fmt; Wd [hidden x ffn])
+ * Eight kernel launches on `stream` (see csrc/qg_slice.cu); intermediates live in a
+ * caller-owned workspace of qg_layer_slice_workspace_bytes() bytes (256-B aligned).
+ * ------------------------------------------------------------------------- */
+typedef struct qg_layer_slice {
+  uint32_t hidden, q_rows, kv_rows, ffn;
+  float eps;
+  const float* norm_weight;
+  int attn_fmt;
+  const uint8_t *wq, *wk, *wv, *wo;
+  const uint8_t *wq_meta, *wk_meta, *wv_meta, *wo_meta;
+  int ffn_fmt;
+  const uint8_t *wg, *wu;
+  const uint8_t *wg_meta, *wu_meta;
+  int down_fmt;
+  const uint8_t* wd;
+  const uint8_t* wd_meta;
+} qg_layer_slice;
+
+/* Device pointers of the slice's intermediate vectors inside a workspace. */
+typedef struct qg_layer_slice_views {
+  float *h, *q, *k, *v, *o, *gate, *up, *act;
+} qg_layer_slice_views;
+
+cudaError_t qg_layer_slice_workspace_bytes(const qg_layer_slice* s, size_t* bytes);
+cudaError_t qg_layer_slice_buffers(const qg_layer_slice* s, void* workspace,
+                                   qg_layer_slice_views* views);
+cudaError_t qg_layer_slice_forward(const qg_layer_slice* s, const float* x, float* out,
+                                   void* workspace, cudaStream_t stream);
+
+/* Decode-step graphs (runtime/apps/mixed_sequence_benchmark_runner/main.cpp:4801-4823
+ * captures, instantiates and uploads one graph, then replays it): everything enqueued
+ * on `stream` between qg_graph_begin and qg_graph_end becomes one graph; the handle
+ * owns it until qg_graph_destroy. */
+typedef struct qg_graph_s* qg_graph;
+cudaError_t qg_graph_begin(cudaStream_t stream);
+cudaError_t qg_graph_end(cudaStream_t stream, qg_graph* out);
+cudaError_t qg_graph_launch(qg_graph graph, cudaStream_t stream);
+cudaError_t qg_graph_destroy(qg_graph graph);
 
 /* Reads the library's device error word (QG_ERR_* bits) for the current device and
  * clears it.  Synchronizes the device.  Returns the cudaError_t of the read. */

@@ -230,6 +230,76 @@ cudaError_t launch_act_prepare(const float* x, uint32_t cols, void* act, cudaStr
   return cudaGetLastError();
 }
 
+// RMSNorm with weights fused with the activation preparation: h = x * inv_rms * w,
+// then h's int8 planes for the GEMVs that read it.  One CTA (the inverse RMS needs
+// the whole vector); h itself is written too when `h` is non-null.
+__global__ void __launch_bounds__(1024) norm_prepare_kernel(const float* __restrict__ x,
+                                                            const float* __restrict__ w,
+                                                            uint32_t n, float eps, float* h,
+                                                            ActChunk* act) {
+  const float sum_sq = block_sum_sq(x, n);
+  const float inv = 1.0f / sqrtf(sum_sq / static_cast<float>(n) + eps);
+  for (uint32_t c = threadIdx.x; c < n / 64u; c += blockDim.x) {
+    float va[32], vb[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      va[i] = x[64u * c + i] * inv * w[64u * c + i];
+      vb[i] = x[64u * c + 32u + i] * inv * w[64u * c + 32u + i];
+    }
+    if (h != nullptr) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        h[64u * c + i] = va[i];
+        h[64u * c + 32u + i] = vb[i];
+      }
+    }
+    XChunk xr;
+    quantize_half(va, xr.ah, xr.al, xr.sa, xr.suma, xr.qh[0], xr.ql[0], xr.qh[1], xr.ql[1]);
+    quantize_half(vb, xr.bh, xr.bl, xr.sb, xr.sumb, xr.qh[2], xr.ql[2], xr.qh[3], xr.ql[3]);
+    store_act_chunk(xr, act + c);
+  }
+}
+
+cudaError_t launch_norm_prepare(const float* x, const float* w, uint32_t n, float eps, float* h,
+                                void* act, cudaStream_t stream) {
+  norm_prepare_kernel<<<1, 1024, 0, stream>>>(x, w, n, eps, h, static_cast<ActChunk*>(act));
+  return cudaGetLastError();
+}
+
+// a = silu(gate) * up fused with a's activation preparation (one thread per 64 columns;
+// the plane scales are per 32 columns, so no cross-thread reduction is needed).
+__global__ void silu_gate_prepare_kernel(const float* __restrict__ gate,
+                                         const float* __restrict__ up, uint32_t n, float* a,
+                                         ActChunk* act) {
+  const uint32_t c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= n / 64u) return;
+  float va[32], vb[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    va[i] = silu(gate[64u * c + i]) * up[64u * c + i];
+    vb[i] = silu(gate[64u * c + 32u + i]) * up[64u * c + 32u + i];
+  }
+  if (a != nullptr) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      a[64u * c + i] = va[i];
+      a[64u * c + 32u + i] = vb[i];
+    }
+  }
+  XChunk xr;
+  quantize_half(va, xr.ah, xr.al, xr.sa, xr.suma, xr.qh[0], xr.ql[0], xr.qh[1], xr.ql[1]);
+  quantize_half(vb, xr.bh, xr.bl, xr.sb, xr.sumb, xr.qh[2], xr.ql[2], xr.qh[3], xr.ql[3]);
+  store_act_chunk(xr, act + c);
+}
+
+cudaError_t launch_silu_gate_prepare(const float* gate, const float* up, uint32_t n, float* a,
+                                     void* act, cudaStream_t stream) {
+  const uint32_t chunks = n / 64u;
+  silu_gate_prepare_kernel<<<(chunks + 63u) / 64u, 64, 0, stream>>>(gate, up, n, a,
+                                                                    static_cast<ActChunk*>(act));
+  return cudaGetLastError();
+}
+
 int device_sm_count() {
   int dev = 0, sms = 0;
   cudaGetDevice(&dev);

@@ -292,13 +292,26 @@ __device__ __forceinline__ void q4_nibble_dot(const uint4 q0, const uint4 q1, co
   sB = planes_value(bh0 + bh1, bl0 + bl1, x.sb * 0.0625f);
 }
 
-// Shared-memory codebook tables of the IQ kernels.
+// Shared-memory codebook tables of the IQ kernels, replicated so that lookups from
+// one warp spread over the 32 banks instead of colliding (random indices into a
+// single copy cost ~3.5 wavefronts per warp-wide lookup):
+//  * 16 copies of a 4-byte table (IQ3_S grid): word (e*16 + k) for lane k = lane % 16,
+//    so lanes k and k+16 share one bank pair -> at most a 2-way conflict;
+//  * 16 copies of an 8-byte table (sign masks): entry (e*16 + k) sits in bank pair k,
+//    one bank pair per lane of a half-warp -> conflict-free;
+//  * 4 copies of the 8-byte IQ2_S expanded grid: copy r = k % 4 occupies only bank
+//    pairs r, r+4, r+8, r+12, so 4 lanes of a half-warp compete for 4 pairs.
 struct IqTables {
-  const uint2* kgrid2;  // IQ2_S: 1024 x 8 bytes 2k
-  const uint2* sign2;   // IQ2_S: 256 x 8 bytes (sign ? 0x0E : 0)
-  const uint32_t* grid3;  // IQ3_S: 512 x 4 magnitudes
-  const uint2* sign3;   // IQ3_S: 256 x 8 bytes (sign ? 0x1E : 0)
+  const uint2* kgrid2;    // IQ2_S: 1024 entries x 4 copies, 8 bytes 2k
+  const uint2* sign2;     // IQ2_S: 256 entries x 16 copies, bytes (sign ? 0x0E : 0)
+  const uint32_t* grid3;  // IQ3_S: 512 entries x 16 copies, 4 magnitudes
+  const uint2* sign3;     // IQ3_S: 256 entries x 16 copies, bytes (sign ? 0x1E : 0)
+  uint32_t k;             // lane % 16
 };
+
+__device__ __forceinline__ uint32_t kgrid2_slot(uint32_t e, uint32_t k) {
+  return ((e >> 2) << 4) | ((e & 3u) << 2) | (k & 3u);
+}
 
 template <int FMT>
 __device__ __forceinline__ float chunk_dot(const uint8_t* rp, const uint8_t* rm, uint32_t c,
@@ -436,8 +449,8 @@ __device__ __forceinline__ float chunk_dot<QG_FMT_IQ2S>(const uint8_t* rp, const
 #pragma unroll
     for (int g = 0; g < 4; ++g) {
       const uint32_t idx = byte_of(gl[ib], g) | ((qhb << (8 - 2 * g)) & 0x300u);
-      const uint2 k2 = t.kgrid2[idx];
-      const uint2 sm = t.sign2[byte_of(sg[ib], g)];
+      const uint2 k2 = t.kgrid2[kgrid2_slot(idx, t.k)];
+      const uint2 sm = t.sign2[(byte_of(sg[ib], g) << 4) | t.k];
       const uint32_t u0 = k2.x ^ sm.x ^ 0x09090909u;
       const uint32_t u1 = k2.y ^ sm.y ^ 0x09090909u;
       ih[g >> 1] = dp4a(u1, H[2 * g + 1], dp4a(u0, H[2 * g], ih[g >> 1]));
@@ -476,13 +489,13 @@ __device__ __forceinline__ float chunk_dot<QG_FMT_IQ3S>(const uint8_t* rp, const
     int ih = 0, il = 0;
 #pragma unroll
     for (int g = 0; g < 4; ++g) {
-      const uint2 sm = t.sign3[byte_of(sg[ib], g)];
+      const uint2 sm = t.sign3[(byte_of(sg[ib], g) << 4) | t.k];
 #pragma unroll
       for (int p = 0; p < 2; ++p) {
         const int sel = 2 * g + p;
         const uint32_t qb = byte_of(qs[2 * ib + (sel >> 2)], sel & 3);
         const uint32_t idx = qb | (((qhb >> sel) & 1u) << 8u);
-        const uint32_t u = t.grid3[idx] ^ 0x11111111u ^ (p ? sm.y : sm.x);
+        const uint32_t u = t.grid3[(idx << 4) | t.k] ^ 0x11111111u ^ (p ? sm.y : sm.x);
         ih = dp4a(u, H[sel], ih);
         il = dp4a(u, Lp[sel], il);
       }
@@ -497,13 +510,24 @@ __device__ __forceinline__ float chunk_dot<QG_FMT_IQ3S>(const uint8_t* rp, const
 }
 
 // Build the IQ tables of a format into shared memory (all threads of the caller).
+__device__ __forceinline__ uint2 sign_bytes(uint32_t s, uint32_t v) {
+  uint32_t lo = 0u, hi = 0u;
+#pragma unroll
+  for (int l = 0; l < 4; ++l) {
+    lo |= ((s >> l) & 1u ? v : 0u) << (8 * l);
+    hi |= ((s >> (l + 4)) & 1u ? v : 0u) << (8 * l);
+  }
+  return make_uint2(lo, hi);
+}
+
 template <int FMT>
 __device__ __forceinline__ void build_iq_tables(uint8_t* base, uint32_t tid, uint32_t n) {
   if (FMT == QG_FMT_IQ2S) {
     uint2* k2 = reinterpret_cast<uint2*>(base);
-    uint2* s2 = k2 + 1024;
-    for (uint32_t i = tid; i < 1024u; i += n) {
-      const uint32_t G = g_iq2s_kgrid[i];
+    uint2* s2 = k2 + 4096;
+    for (uint32_t i = tid; i < 4096u; i += n) {
+      const uint32_t e = ((i >> 4) << 2) | ((i >> 2) & 3u);  // inverse of kgrid2_slot
+      const uint32_t G = g_iq2s_kgrid[e];
       uint32_t lo = 0u, hi = 0u;
 #pragma unroll
       for (int l = 0; l < 4; ++l) {
@@ -512,46 +536,31 @@ __device__ __forceinline__ void build_iq_tables(uint8_t* base, uint32_t tid, uin
       }
       k2[i] = make_uint2(lo, hi);
     }
-    for (uint32_t i = tid; i < 256u; i += n) {
-      uint32_t lo = 0u, hi = 0u;
-#pragma unroll
-      for (int l = 0; l < 4; ++l) {
-        lo |= ((i >> l) & 1u ? 0x0eu : 0u) << (8 * l);
-        hi |= ((i >> (l + 4)) & 1u ? 0x0eu : 0u) << (8 * l);
-      }
-      s2[i] = make_uint2(lo, hi);
-    }
+    for (uint32_t i = tid; i < 4096u; i += n) s2[i] = sign_bytes(i >> 4, 0x0eu);
   } else if (FMT == QG_FMT_IQ3S) {
     uint32_t* g3 = reinterpret_cast<uint32_t*>(base);
-    uint2* s3 = reinterpret_cast<uint2*>(base + 2048);
-    for (uint32_t i = tid; i < 512u; i += n) g3[i] = g_iq3s_grid[i];
-    for (uint32_t i = tid; i < 256u; i += n) {
-      uint32_t lo = 0u, hi = 0u;
-#pragma unroll
-      for (int l = 0; l < 4; ++l) {
-        lo |= ((i >> l) & 1u ? 0x1eu : 0u) << (8 * l);
-        hi |= ((i >> (l + 4)) & 1u ? 0x1eu : 0u) << (8 * l);
-      }
-      s3[i] = make_uint2(lo, hi);
-    }
+    uint2* s3 = reinterpret_cast<uint2*>(base + 32768);
+    for (uint32_t i = tid; i < 8192u; i += n) g3[i] = g_iq3s_grid[i >> 4];
+    for (uint32_t i = tid; i < 4096u; i += n) s3[i] = sign_bytes(i >> 4, 0x1eu);
   }
 }
 
 template <int FMT>
-__device__ __forceinline__ IqTables iq_tables(const uint8_t* base) {
+__device__ __forceinline__ IqTables iq_tables(const uint8_t* base, uint32_t lane) {
   IqTables t{};
+  t.k = lane & 15u;
   if (FMT == QG_FMT_IQ2S) {
     t.kgrid2 = reinterpret_cast<const uint2*>(base);
-    t.sign2 = t.kgrid2 + 1024;
+    t.sign2 = t.kgrid2 + 4096;
   } else if (FMT == QG_FMT_IQ3S) {
     t.grid3 = reinterpret_cast<const uint32_t*>(base);
-    t.sign3 = reinterpret_cast<const uint2*>(base + 2048);
+    t.sign3 = reinterpret_cast<const uint2*>(base + 32768);
   }
   return t;
 }
 
 constexpr uint32_t iq_table_bytes(int fmt) {
-  return fmt == QG_FMT_IQ2S ? 10240u : fmt == QG_FMT_IQ3S ? 4096u : 0u;
+  return fmt == QG_FMT_IQ2S ? 65536u : fmt == QG_FMT_IQ3S ? 65536u : 0u;
 }
 
 // A prepared activation: x quantized once (qg_act_prepare) into one 176-byte record

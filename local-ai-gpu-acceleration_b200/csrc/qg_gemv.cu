@@ -36,6 +36,17 @@ __device__ unsigned int g_error_word = 0u;
 __device__ uint16_t g_iq2s_kgrid[1024] = {QG_IQ2S_KGRID_VALUES};
 __device__ uint32_t g_iq3s_grid[512] = {QG_IQ3S_GRID_VALUES};
 
+// One weight matrix of a multi-matrix launch (same format and cols): its tiles are
+// [tile_end of the previous segment, tile_end).
+struct GemvSeg {
+  const uint8_t* payload;
+  const uint8_t* meta;
+  float* y;
+  uint32_t rows;
+  uint32_t tile_end;
+};
+constexpr int kMaxSegs = 3;
+
 struct GemvArgs {
   const uint8_t* payload;
   const uint8_t* meta;
@@ -67,7 +78,21 @@ struct GemvArgs {
   uint32_t stage_shift;   // log2(passes per stage)
   uint32_t x_vec;         // x is 16-B aligned (vector loads)
   const ActChunk* xq;     // prepared activation (qg_act_prepare), or null: quantize x here
+  GemvSeg seg[kMaxSegs];  // tiled kernel: the matrices of this launch (seg[0] = payload/meta/y)
+  uint32_t nseg;
 };
+
+// Segment of tile `tile` and the tile's first row inside that segment.
+__device__ __forceinline__ uint32_t tile_segment(const GemvArgs& a, uint32_t tile,
+                                                 uint32_t& row0) {
+  uint32_t s = 0, begin = 0;
+  while (s + 1u < a.nseg && tile >= a.seg[s].tile_end) {
+    begin = a.seg[s].tile_end;
+    ++s;
+  }
+  row0 = (tile - begin) * a.rows_per_tile;
+  return s;
+}
 
 template <int FMT>
 __device__ __forceinline__ void issue_tile(const GemvArgs& a, uint8_t* stage, uint64_t* bar,
@@ -136,7 +161,7 @@ __global__ void __launch_bounds__(512, 1) gemv_staged_kernel(const GemvArgs a) {
 
   // Codebooks into shared memory (overlaps the first TMA loads).
   build_iq_tables<FMT>(smem + a.table_off, tid, nthreads);
-  const IqTables tables = iq_tables<FMT>(smem + a.table_off);
+  const IqTables tables = iq_tables<FMT>(smem + a.table_off, tid & 31u);
   XChunk xr;
   if (a.xq != nullptr) {
     load_act_chunk(a.xq + c, xr);
@@ -255,17 +280,17 @@ __global__ void __launch_bounds__(256) gemv_rowwise_kernel(const GemvArgs a) {
 // pack (fewer at its end).  The last stage of a pack may end off a 16-B boundary:
 // its tail bytes are copied here, before the arrive that publishes the stage.
 template <int FMT>
-__device__ __forceinline__ void tiled_issue(const GemvArgs& a, uint8_t* st, uint64_t* bar,
-                                            uint32_t row_begin, uint64_t policy) {
+__device__ __forceinline__ void tiled_issue(const GemvArgs& a, const GemvSeg& g, uint8_t* st,
+                                            uint64_t* bar, uint32_t row_begin, uint64_t policy) {
   constexpr uint32_t PB = FmtTraits<FMT>::payload_bytes;
   constexpr uint32_t MB = FmtTraits<FMT>::meta_bytes;
   const uint32_t bpr = a.cols >> 8;
   uint32_t nr = 0u;
-  if (row_begin < a.rows) nr = min(a.stage_rows, a.rows - row_begin);
+  if (row_begin < g.rows) nr = min(a.stage_rows, g.rows - row_begin);
   const uint32_t pb = nr * bpr * PB, mb = nr * bpr * MB;
   const uint32_t pb16 = pb & ~15u, mb16 = mb & ~15u;
-  const uint8_t* src = a.payload + static_cast<uint64_t>(row_begin) * bpr * PB;
-  const uint8_t* msrc = a.meta + static_cast<uint64_t>(row_begin) * bpr * MB;
+  const uint8_t* src = g.payload + static_cast<uint64_t>(row_begin) * bpr * PB;
+  const uint8_t* msrc = g.meta + static_cast<uint64_t>(row_begin) * bpr * MB;
   for (uint32_t o = pb16; o < pb; ++o) st[o] = src[o];
   if (MB != 0u) {
     for (uint32_t o = mb16; o < mb; ++o) st[a.meta_off + o] = msrc[o];
@@ -322,13 +347,15 @@ __global__ void __launch_bounds__(544, 1) gemv_tiled_kernel(const GemvArgs a) {
       bool ok = true;
       uint32_t s = 0, ephase = 0, issued = 0;
       for (uint32_t i = 0; i < n_my && ok; ++i) {
-        const uint32_t row0 = (first + i * stride) * a.rows_per_tile;
+        uint32_t row0;
+        const GemvSeg& g = a.seg[tile_segment(a, first + i * stride, row0)];
         for (uint32_t j = 0; j < loads_per_tile; ++j) {
           if (issued >= S) {
             ok = mbar_wait_bounded(&empty[s], ephase);
             if (!ok) break;
           }
-          tiled_issue<FMT>(a, stages + s * a.stage_bytes, &full[s], row0 + j * a.stage_rows, policy);
+          tiled_issue<FMT>(a, g, stages + s * a.stage_bytes, &full[s], row0 + j * a.stage_rows,
+                           policy);
           ++issued;
           if (++s == S) {
             s = 0;
@@ -360,7 +387,7 @@ __global__ void __launch_bounds__(544, 1) gemv_tiled_kernel(const GemvArgs a) {
   const uint32_t Q = a.stage_rows / a.rpp;
 
   build_iq_tables<FMT>(smem + a.table_off, tid, nconsumers);
-  const IqTables tables = iq_tables<FMT>(smem + a.table_off);
+  const IqTables tables = iq_tables<FMT>(smem + a.table_off, tid & 31u);
   XChunk xr;
   if (a.xq != nullptr) {
     load_act_chunk(a.xq + c, xr);
@@ -373,8 +400,9 @@ __global__ void __launch_bounds__(544, 1) gemv_tiled_kernel(const GemvArgs a) {
   uint32_t s = 0, phase = 0;
   bool failed = false;
   for (uint32_t i = 0; i < n_my && !failed; ++i) {
-    const uint32_t row0 = (first + i * stride) * a.rows_per_tile;
-    const uint32_t nrows = min(a.rows_per_tile, a.rows - row0);
+    uint32_t row0;
+    const GemvSeg& g = a.seg[tile_segment(a, first + i * stride, row0)];
+    const uint32_t nrows = min(a.rows_per_tile, g.rows - row0);
     float* rb = red + (i & 1u) * (a.rows_per_tile * gpr);
     for (uint32_t j = 0; j < loads_per_tile; ++j) {
       if (!mbar_wait_bounded(&full[s], phase)) failed = true;
@@ -406,7 +434,7 @@ __global__ void __launch_bounds__(544, 1) gemv_tiled_kernel(const GemvArgs a) {
       for (uint32_t g = 0; g < gpr; ++g) v += rb[t * gpr + g];
       const uint32_t row = row0 + t;
       if (a.residual != nullptr) v += a.residual[row];
-      a.y[row] = v;
+      g.y[row] = v;
       if (a.kv != nullptr && row < a.active_pages && a.kv_words > 0u && a.page_words > 0u) {
         const uint64_t kb = static_cast<uint64_t>(row) * a.page_words;
         const uint64_t ko = (tok + row) % a.page_words;
@@ -522,6 +550,8 @@ cudaError_t launch_gemv_fmt(GemvArgs a, cudaStream_t stream) {
     if (plan.tiled && plan.smem_bytes <= static_cast<uint32_t>(dev.max_smem_optin)) {
       fill_args(a, plan);
       a.tma_ok = 1u;
+      a.nseg = 1u;
+      a.seg[0] = GemvSeg{a.payload, a.meta, a.y, a.rows, plan.num_tiles};
       const cudaError_t e = ensure_smem_attr(gemv_tiled_kernel<FMT>, dev.max_smem_optin);
       if (e != cudaSuccess) return e;
       const uint32_t per_sm = resident_ctas(gemv_tiled_kernel<FMT>, plan.threads, plan.smem_bytes);
@@ -543,6 +573,58 @@ cudaError_t launch_gemv_fmt(GemvArgs a, cudaStream_t stream) {
   const uint32_t per_sm = resident_ctas(gemv_staged_kernel<FMT>, plan.threads, plan.smem_bytes);
   const uint32_t grid = std::max(1u, std::min(plan.num_tiles, per_sm * dev.sms));
   gemv_staged_kernel<FMT><<<grid, plan.threads, plan.smem_bytes, stream>>>(a);
+  return cudaGetLastError();
+}
+
+// Several matrices of one format and width that read the same x, in one launch (the
+// Q/K/V projections, gate/up).  Falls back to one launch per matrix when a matrix is
+// not 16-B aligned or the shape cannot use the tiled kernel.
+template <int FMT>
+cudaError_t launch_multi_fmt(GemvArgs a, uint32_t nseg, const GemvSeg* segs, cudaStream_t stream) {
+  constexpr uint32_t MB = FmtTraits<FMT>::meta_bytes;
+  const DeviceInfo dev = device_info();
+  a.tpr = a.cols / 64u;
+  a.x_vec = (reinterpret_cast<uintptr_t>(a.x) & 15u) == 0u ? 1u : 0u;
+  bool aligned = a.cols >= 256u && a.tpr <= 512u;
+  uint32_t total_rows = 0;
+  for (uint32_t k = 0; k < nseg; ++k) {
+    aligned = aligned && (reinterpret_cast<uintptr_t>(segs[k].payload) & 15u) == 0u &&
+              (MB == 0u || (reinterpret_cast<uintptr_t>(segs[k].meta) & 15u) == 0u);
+    total_rows += segs[k].rows;
+  }
+  GemvPlan plan{};
+  if (aligned) plan = plan_gemv(FMT, total_rows, a.cols, dev.sms);
+  if (!aligned || !plan.tiled || plan.smem_bytes > static_cast<uint32_t>(dev.max_smem_optin)) {
+    for (uint32_t k = 0; k < nseg; ++k) {
+      GemvArgs b = a;
+      b.payload = segs[k].payload;
+      b.meta = segs[k].meta;
+      b.y = segs[k].y;
+      b.rows = segs[k].rows;
+      const cudaError_t e = launch_gemv_fmt<FMT>(b, stream);
+      if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+  }
+  fill_args(a, plan);
+  a.tma_ok = 1u;
+  a.nseg = nseg;
+  uint32_t tiles = 0;
+  for (uint32_t k = 0; k < nseg; ++k) {
+    a.seg[k] = segs[k];
+    tiles += (segs[k].rows + plan.rows_per_tile - 1u) / plan.rows_per_tile;
+    a.seg[k].tile_end = tiles;
+  }
+  a.num_tiles = tiles;
+  a.payload = segs[0].payload;
+  a.meta = segs[0].meta;
+  a.y = segs[0].y;
+  a.rows = segs[0].rows;
+  const cudaError_t e = ensure_smem_attr(gemv_tiled_kernel<FMT>, dev.max_smem_optin);
+  if (e != cudaSuccess) return e;
+  const uint32_t per_sm = resident_ctas(gemv_tiled_kernel<FMT>, plan.threads, plan.smem_bytes);
+  const uint32_t grid = std::max(1u, std::min(tiles, per_sm * dev.sms));
+  gemv_tiled_kernel<FMT><<<grid, plan.threads, plan.smem_bytes, stream>>>(a);
   return cudaGetLastError();
 }
 
@@ -596,7 +678,8 @@ GemvPlan plan_gemv(int fmt, uint32_t rows, uint32_t cols, int sms) {
     return p;
   }
   const uint32_t q_align = q;
-  while (q < 16u && 2u * q * p.rpp * (row_bytes + row_meta) <= 16384u) q <<= 1;
+  const uint32_t stage_target = iq_table_bytes(fmt) ? 8192u : 16384u;
+  while (q < 16u && 2u * q * p.rpp * (row_bytes + row_meta) <= stage_target) q <<= 1;
   const uint32_t resident = static_cast<uint32_t>(sms) * 2u;
   uint32_t P = 32u;
   while (P > 4u && (rows + P * p.rpp - 1u) / (P * p.rpp) < 2u * resident) P >>= 1;
@@ -610,7 +693,8 @@ GemvPlan plan_gemv(int fmt, uint32_t rows, uint32_t cols, int sms) {
   const uint32_t pay = p.stage_rows * row_bytes, met = p.stage_rows * row_meta;
   p.meta_off = (pay + 127u) & ~127u;
   p.stage_bytes = MB ? ((p.meta_off + met + 127u) & ~127u) : ((pay + 127u) & ~127u);
-  p.stages = std::max(2u, std::min(8u, (96u * 1024u) / p.stage_bytes));
+  const uint32_t budget = iq_table_bytes(fmt) ? 40u * 1024u : 96u * 1024u;
+  p.stages = std::max(2u, std::min(8u, budget / p.stage_bytes));
   p.threads += 32u;  // producer warp
   plan_smem(fmt, tpr, p);
   p.grid = std::max(1u, std::min(p.num_tiles, static_cast<uint32_t>(sms) * ctas_per_sm(p)));
@@ -669,6 +753,32 @@ cudaError_t launch_gemv(int fmt, const uint8_t* payload, const uint8_t* meta, co
     case QG_FMT_Q5K: return launch_gemv_fmt<QG_FMT_Q5K>(a, stream);
     case QG_FMT_IQ2S: return launch_gemv_fmt<QG_FMT_IQ2S>(a, stream);
     case QG_FMT_IQ3S: return launch_gemv_fmt<QG_FMT_IQ3S>(a, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t launch_gemv_multi(int fmt, uint32_t nseg, const uint8_t* const* payload,
+                              const uint8_t* const* meta, float* const* y, const uint32_t* rows,
+                              uint32_t cols, const float* x, const void* act,
+                              cudaStream_t stream) {
+  if (nseg == 0u || nseg > static_cast<uint32_t>(kMaxSegs)) return cudaErrorInvalidValue;
+  GemvSeg segs[kMaxSegs];
+  for (uint32_t k = 0; k < nseg; ++k) {
+    segs[k] = GemvSeg{payload[k], meta ? meta[k] : nullptr, y[k], rows[k], 0u};
+  }
+  GemvArgs a{};
+  a.x = x;
+  a.xq = static_cast<const ActChunk*>(act);
+  a.cols = cols;
+  switch (fmt) {
+    case QG_FMT_Q4K_RAW: return launch_multi_fmt<QG_FMT_Q4K_RAW>(a, nseg, segs, stream);
+    case QG_FMT_Q4K_SPLIT_PREDECODED: return launch_multi_fmt<QG_FMT_Q4K_SPLIT_PREDECODED>(a, nseg, segs, stream);
+    case QG_FMT_Q4K_SPLIT_HALF: return launch_multi_fmt<QG_FMT_Q4K_SPLIT_HALF>(a, nseg, segs, stream);
+    case QG_FMT_Q4K_SPLIT_COMPACT: return launch_multi_fmt<QG_FMT_Q4K_SPLIT_COMPACT>(a, nseg, segs, stream);
+    case QG_FMT_Q4K_SPLIT_NATIVE: return launch_multi_fmt<QG_FMT_Q4K_SPLIT_NATIVE>(a, nseg, segs, stream);
+    case QG_FMT_Q5K: return launch_multi_fmt<QG_FMT_Q5K>(a, nseg, segs, stream);
+    case QG_FMT_IQ2S: return launch_multi_fmt<QG_FMT_IQ2S>(a, nseg, segs, stream);
+    case QG_FMT_IQ3S: return launch_multi_fmt<QG_FMT_IQ3S>(a, nseg, segs, stream);
     default: return cudaErrorInvalidValue;
   }
 }

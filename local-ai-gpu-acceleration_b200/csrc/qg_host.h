@@ -29,6 +29,11 @@ cudaError_t launch_gemv(int fmt, const uint8_t* payload, const uint8_t* meta, co
                         const uint32_t* token, uint64_t kv_words, uint32_t page_words,
                         uint32_t active_pages, uint32_t rows, uint32_t cols, cudaStream_t stream);
 
+// Up to 3 matrices of one format and width reading the same x, in one launch.
+cudaError_t launch_gemv_multi(int fmt, uint32_t nseg, const uint8_t* const* payload,
+                              const uint8_t* const* meta, float* const* y, const uint32_t* rows,
+                              uint32_t cols, const float* x, const void* act, cudaStream_t stream);
+
 // Bytes of a prepared activation of `cols` values (176 per 64 columns).
 inline size_t act_bytes(uint32_t cols) { return static_cast<size_t>(cols / 64u) * 176u; }
 cudaError_t launch_act_prepare(const float* x, uint32_t cols, void* act, cudaStream_t stream);
@@ -50,6 +55,13 @@ cudaError_t launch_weighted_rmsnorm(const float* x, const float* w, uint32_t n, 
 
 cudaError_t launch_silu_gate(const float* gate, const float* up, uint32_t n, float* h,
                              cudaStream_t stream);
+
+// h = x * inv_rms(x) * w (+ h's prepared activation); one CTA.
+cudaError_t launch_norm_prepare(const float* x, const float* w, uint32_t n, float eps, float* h,
+                                void* act, cudaStream_t stream);
+// a = silu(gate) * up (+ a's prepared activation).
+cudaError_t launch_silu_gate_prepare(const float* gate, const float* up, uint32_t n, float* a,
+                                     void* act, cudaStream_t stream);
 
 int device_sm_count();
 

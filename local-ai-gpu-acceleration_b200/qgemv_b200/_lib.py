@@ -61,6 +61,13 @@ SIGNATURES: dict[str, list] = {
     "qg_argmax_token": [P, U32, P, U32, U32, U32, P],
     "qg_get_error": [P],
     "qg_gemv_plan": [c_int, U32, U32, P, P, P, P],
+    "qg_layer_slice_workspace_bytes": [P, P],
+    "qg_layer_slice_buffers": [P, P, P],
+    "qg_layer_slice_forward": [P, P, P, P, P],
+    "qg_graph_begin": [P],
+    "qg_graph_end": [P, P],
+    "qg_graph_launch": [P, P],
+    "qg_graph_destroy": [P],
 }
 
 _LIB: ctypes.CDLL | None = None

@@ -92,3 +92,12 @@ def test_feedback_cache_validation():
 
 def test_get_error_rejects_null():
     assert qgemv_b200.call("qg_get_error", None) == INVALID_VALUE
+
+
+def test_layer_slice_rejects_bad_dims():
+    from qgemv_b200.slice import LayerSliceC
+
+    c = LayerSliceC()
+    c.hidden, c.q_rows, c.kv_rows, c.ffn = 4096, 4096, 1024, 1000  # ffn not a multiple of 256
+    n = ctypes.c_size_t(0)
+    assert qgemv_b200.call("qg_layer_slice_workspace_bytes", ctypes.byref(c), ctypes.byref(n)) == 1

@@ -1,0 +1,101 @@
+"""Layer slice: every stage against the oracle, fed the GPU's own
+input to that stage (stage-wise parity, as the reference's mixed runner checks each
+stage, runtime/apps/mixed_sequence_benchmark_runner/main.cpp:2729-2790), the whole
+slice against an all-oracle chain, and graph capture/replay."""
+
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+from qgemv_b200 import packs
+from qgemv_b200.slice import LayerSlice, StepGraph
+from test_gpu_parity import assert_rows_close, row_tol
+
+pytestmark = pytest.mark.gpu
+
+
+def oracle_weighted_rmsnorm(port, x, w, eps):
+    y = np.empty_like(x)
+    port.lib.orc_weighted_rmsnorm(x.ctypes.data, w.ctypes.data, x.size, ctypes.c_float(eps), y.ctypes.data)
+    return y
+
+
+def oracle_silu_gate(port, g, u):
+    h = np.empty_like(g)
+    port.lib.orc_silu_gate(g.ctypes.data, u.ctypes.data, g.size, h.ctypes.data)
+    return h
+
+
+def stage_check(port, sl, name, x_in, y_gpu):
+    pk = sl.host[name]
+    rows, cols = sl.shapes[name]
+    want = port.matvec(pk.fmt, pk.payload, pk.meta, x_in, rows, cols)
+    assert_rows_close(y_gpu, want, row_tol(port, pk.fmt, pk.payload, pk.meta, x_in, rows, cols))
+
+
+@pytest.mark.parametrize("dims", [
+    dict(hidden=512, q_rows=512, kv_rows=256, ffn=1536),
+    dict(hidden=4096, q_rows=4096, kv_rows=1024, ffn=14336),
+])
+def test_layer_slice_stagewise(cuda, port, dims):
+    sl = LayerSlice(**dims, seed=5, keep_host=True)
+    x = packs.synthetic_activation(dims["hidden"], 77)
+    xd = torch.from_numpy(x).to(cuda)
+    out = sl.forward(xd)
+    torch.cuda.synchronize()
+    v = {k: t.cpu().numpy() for k, t in sl.views().items()}
+    h_want = oracle_weighted_rmsnorm(port, x, sl.norm_host, sl.eps)
+    np.testing.assert_allclose(v["h"], h_want, rtol=2e-6, atol=1e-6)
+    if dims["hidden"] <= 512:
+        stage_check(port, sl, "wq", v["h"], v["q"])
+        stage_check(port, sl, "wk", v["h"], v["k"])
+        stage_check(port, sl, "wv", v["h"], v["v"])
+        stage_check(port, sl, "wo", v["q"], v["o"])
+        stage_check(port, sl, "wg", v["o"], v["gate"])
+        stage_check(port, sl, "wu", v["o"], v["up"])
+    np.testing.assert_allclose(v["act"], oracle_silu_gate(port, v["gate"], v["up"]), rtol=1e-5, atol=1e-6)
+    # last stage on the full rows (down projection + residual)
+    pk = sl.host["wd"]
+    rows, cols = sl.shapes["wd"]
+    want = x + port.matvec(pk.fmt, pk.payload, pk.meta, v["act"], rows, cols)
+    tol = row_tol(port, pk.fmt, pk.payload, pk.meta, v["act"], rows, cols) + 1e-6 * np.abs(x)
+    assert_rows_close(out.cpu().numpy(), want, tol)
+
+
+def test_layer_slice_end_to_end_vs_oracle_chain(cuda, port):
+    """Whole slice vs an all-oracle chain (fp32 reference GEMVs throughout)."""
+    dims = dict(hidden=512, q_rows=512, kv_rows=256, ffn=1536)
+    sl = LayerSlice(**dims, seed=9, keep_host=True)
+    x = packs.synthetic_activation(dims["hidden"], 99)
+    out = sl.forward(torch.from_numpy(x).to(cuda)).cpu().numpy()
+
+    def mv(name, v):
+        pk = sl.host[name]
+        return port.matvec(pk.fmt, pk.payload, pk.meta, v, *sl.shapes[name])
+
+    h = oracle_weighted_rmsnorm(port, x, sl.norm_host, sl.eps)
+    q = mv("wq", h)
+    o = mv("wo", q)
+    a = oracle_silu_gate(port, mv("wg", o), mv("wu", o))
+    want = x + mv("wd", a)
+    # errors of ~3e-5 relative per GEMV compound through four GEMVs
+    scale = np.abs(want).max()
+    assert np.abs(out - want).max() <= 2e-3 * scale
+
+
+def test_layer_slice_graph_replay_matches_eager(cuda):
+    dims = dict(hidden=4096, q_rows=4096, kv_rows=1024, ffn=14336)
+    sl = LayerSlice(**dims, seed=1)
+    x = torch.randn(dims["hidden"], device=cuda)
+    eager = sl.forward(x).clone()
+    out = torch.empty_like(x)
+    stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
+    g = StepGraph(stream, lambda: sl.forward(x, out, stream))
+    for _ in range(3):
+        g.launch()
+    stream.synchronize()
+    g.close()
+    assert torch.equal(out, eager)
