@@ -265,7 +265,8 @@ cudaError_t qg_act_bytes(uint32_t cols, size_t* bytes) {
 
 cudaError_t qg_act_prepare(const float* x, uint32_t cols, void* act, cudaStream_t stream) {
   if (x == nullptr || act == nullptr || cols == 0u || (cols % 256u) != 0u ||
-      (reinterpret_cast<uintptr_t>(act) & 15u) != 0u) {
+      (reinterpret_cast<uintptr_t>(act) & 15u) != 0u ||
+      (reinterpret_cast<uintptr_t>(x) & 7u) != 0u) {
     return cudaErrorInvalidValue;
   }
   return qg::launch_act_prepare(x, cols, act, stream);

@@ -26,6 +26,8 @@ __global__ void __launch_bounds__(1024) argmax_token_kernel(const float* __restr
                                                             uint32_t modulus) {
   __shared__ float sv[32];
   __shared__ uint32_t si[32];
+  pdl_wait();
+  pdl_trigger();
   float bv = -3.4028234663852886e38f;
   uint32_t bi = 0u;
   const uint32_t tid = threadIdx.x;
@@ -71,8 +73,7 @@ __global__ void __launch_bounds__(1024) argmax_token_kernel(const float* __restr
 
 cudaError_t launch_argmax_token(const float* v, uint32_t n, uint32_t* token, uint32_t offset,
                                 uint32_t add_token, uint32_t modulus, cudaStream_t stream) {
-  argmax_token_kernel<<<1, 1024, 0, stream>>>(v, n, token, offset, add_token, modulus);
-  return cudaGetLastError();
+  return launch_k(argmax_token_kernel, 1, 1024, 0, stream, v, n, token, offset, add_token, modulus);
 }
 
 // ---------------------------------------------------------------------------
@@ -118,6 +119,8 @@ __global__ void __launch_bounds__(256) feedback_kernel(uint32_t mode, const floa
                                                        const float* gate, uint32_t rows,
                                                        uint32_t cols, uint32_t cache_cols,
                                                        float eps, uint32_t accumulate) {
+  pdl_wait();
+  pdl_trigger();
   const float sum_sq = block_sum_sq(logits, rows);
   const float inv = 1.0f / sqrtf(sum_sq / static_cast<float>(rows) + eps);
   const uint32_t c = blockIdx.x * blockDim.x + threadIdx.x;
@@ -145,9 +148,8 @@ cudaError_t launch_feedback(uint32_t mode, const float* logits, float* act, floa
                             float eps, uint32_t accumulate, cudaStream_t stream) {
   if (rows == 0u || cols == 0u) return cudaSuccess;  // the reference kernels return early
   const uint32_t blocks = (cols + 255u) / 256u;
-  feedback_kernel<<<blocks, 256, 0, stream>>>(mode, logits, act, cache, gate, rows, cols,
-                                              cache_cols, eps, accumulate);
-  return cudaGetLastError();
+  return launch_k(feedback_kernel, blocks, 256, 0, stream, mode, logits, act, cache, gate, rows, cols,
+                  cache_cols, eps, accumulate);
 }
 
 // ---------------------------------------------------------------------------
@@ -155,6 +157,8 @@ cudaError_t launch_feedback(uint32_t mode, const float* logits, float* act, floa
 template <int FMT>
 __global__ void dequant_kernel(const uint8_t* payload, const uint8_t* meta, uint64_t first_block,
                                uint64_t count, float* out) {
+  pdl_wait();
+  pdl_trigger();
   const uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= count * 256u) return;
   out[i] = dequant_value<FMT>(payload, meta, first_block + (i >> 8), static_cast<uint32_t>(i & 255u));
@@ -166,7 +170,7 @@ cudaError_t launch_dequant(int fmt, const uint8_t* payload, const uint8_t* meta,
   const uint32_t blocks = static_cast<uint32_t>((total + 255u) / 256u);
   switch (fmt) {
 #define QG_DQ(F) \
-  case F: dequant_kernel<F><<<blocks, 256, 0, stream>>>(payload, meta, first_block, count, out); break;
+  case F: return launch_k(dequant_kernel<F>, blocks, 256, 0, stream, payload, meta, first_block, count, out);
     QG_DQ(QG_FMT_Q4K_RAW)
     QG_DQ(QG_FMT_Q4K_SPLIT_PREDECODED)
     QG_DQ(QG_FMT_Q4K_SPLIT_HALF)
@@ -178,7 +182,6 @@ cudaError_t launch_dequant(int fmt, const uint8_t* payload, const uint8_t* meta,
 #undef QG_DQ
     default: return cudaErrorInvalidValue;
   }
-  return cudaGetLastError();
 }
 
 // ---------------------------------------------------------------------------
@@ -187,6 +190,8 @@ cudaError_t launch_dequant(int fmt, const uint8_t* payload, const uint8_t* meta,
 // y = x / sqrt(mean(x^2) + eps) * w   (one CTA; n is the hidden size)
 __global__ void __launch_bounds__(1024) weighted_rmsnorm_kernel(const float* x, const float* w,
                                                                 uint32_t n, float eps, float* y) {
+  pdl_wait();
+  pdl_trigger();
   const float sum_sq = block_sum_sq(x, n);
   const float inv = 1.0f / sqrtf(sum_sq / static_cast<float>(n) + eps);
   for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) y[i] = x[i] * inv * w[i];
@@ -194,110 +199,99 @@ __global__ void __launch_bounds__(1024) weighted_rmsnorm_kernel(const float* x, 
 
 cudaError_t launch_weighted_rmsnorm(const float* x, const float* w, uint32_t n, float eps,
                                     float* y, cudaStream_t stream) {
-  weighted_rmsnorm_kernel<<<1, 1024, 0, stream>>>(x, w, n, eps, y);
-  return cudaGetLastError();
+  return launch_k(weighted_rmsnorm_kernel, 1, 1024, 0, stream, x, w, n, eps, y);
 }
 
 // h = silu(gate) * up
 __global__ void silu_gate_kernel(const float* gate, const float* up, uint32_t n, float* h) {
+  pdl_wait();
+  pdl_trigger();
   const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) h[i] = silu(gate[i]) * up[i];
 }
 
 cudaError_t launch_silu_gate(const float* gate, const float* up, uint32_t n, float* h,
                              cudaStream_t stream) {
-  silu_gate_kernel<<<(n + 255u) / 256u, 256, 0, stream>>>(gate, up, n, h);
-  return cudaGetLastError();
+  return launch_k(silu_gate_kernel, (n + 255u) / 256u, 256, 0, stream, gate, up, n, h);
 }
 
 // ---------------------------------------------------------------------------
 // Activation preparation: x -> one ActChunk (int8 planes + scales + sums) per 64
-// columns, read by every GEMV CTA instead of re-quantizing x in each of them.
-__global__ void act_prepare_kernel(const float* __restrict__ x, uint32_t chunks, ActChunk* out,
-                                   uint32_t x_vec) {
-  const uint32_t c = blockIdx.x * blockDim.x + threadIdx.x;
+// columns, read by every GEMV CTA instead of re-quantizing x in each of them.  One
+// warp per chunk.
+__global__ void act_prepare_kernel(const float* __restrict__ x, uint32_t chunks, ActChunk* out) {
+  pdl_wait();
+  pdl_trigger();
+  const uint32_t c = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   if (c >= chunks) return;
-  XChunk xr;
-  load_x_chunk(x + 64u * c, x_vec != 0u, xr);
-  store_act_chunk(xr, out + c);
+  const uint32_t lane = threadIdx.x & 31u;
+  const float2 v = *reinterpret_cast<const float2*>(x + 64u * c + 2u * lane);
+  warp_prepare_chunk(v.x, v.y, out + c);
 }
 
 cudaError_t launch_act_prepare(const float* x, uint32_t cols, void* act, cudaStream_t stream) {
   const uint32_t chunks = cols / 64u;
-  const uint32_t vec = (reinterpret_cast<uintptr_t>(x) & 15u) == 0u ? 1u : 0u;
-  act_prepare_kernel<<<(chunks + 63u) / 64u, 64, 0, stream>>>(x, chunks,
-                                                              static_cast<ActChunk*>(act), vec);
-  return cudaGetLastError();
+  if ((reinterpret_cast<uintptr_t>(x) & 7u) != 0u) {
+    // 8-B alignment is needed for the float2 loads; copy-free fallback: in-kernel path
+    return cudaErrorInvalidValue;
+  }
+  return launch_k(act_prepare_kernel, (chunks + 3u) / 4u, 128, 0, stream, x, chunks,
+                  static_cast<ActChunk*>(act));
 }
 
 // RMSNorm with weights fused with the activation preparation: h = x * inv_rms * w,
 // then h's int8 planes for the GEMVs that read it.  One CTA (the inverse RMS needs
-// the whole vector); h itself is written too when `h` is non-null.
+// the whole vector), one warp per 64-column chunk; h itself is written too when `h`
+// is non-null.
 __global__ void __launch_bounds__(1024) norm_prepare_kernel(const float* __restrict__ x,
                                                             const float* __restrict__ w,
                                                             uint32_t n, float eps, float* h,
                                                             ActChunk* act) {
+  pdl_wait();
+  pdl_trigger();
   const float sum_sq = block_sum_sq(x, n);
   const float inv = 1.0f / sqrtf(sum_sq / static_cast<float>(n) + eps);
-  for (uint32_t c = threadIdx.x; c < n / 64u; c += blockDim.x) {
-    float va[32], vb[32];
-#pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      va[i] = x[64u * c + i] * inv * w[64u * c + i];
-      vb[i] = x[64u * c + 32u + i] * inv * w[64u * c + 32u + i];
-    }
+  const uint32_t lane = threadIdx.x & 31u;
+  for (uint32_t c = threadIdx.x >> 5; c < n / 64u; c += blockDim.x >> 5) {
+    const uint32_t i = 64u * c + 2u * lane;
+    const float v0 = x[i] * inv * w[i], v1 = x[i + 1u] * inv * w[i + 1u];
     if (h != nullptr) {
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        h[64u * c + i] = va[i];
-        h[64u * c + 32u + i] = vb[i];
-      }
+      h[i] = v0;
+      h[i + 1u] = v1;
     }
-    XChunk xr;
-    quantize_half(va, xr.ah, xr.al, xr.sa, xr.suma, xr.qh[0], xr.ql[0], xr.qh[1], xr.ql[1]);
-    quantize_half(vb, xr.bh, xr.bl, xr.sb, xr.sumb, xr.qh[2], xr.ql[2], xr.qh[3], xr.ql[3]);
-    store_act_chunk(xr, act + c);
+    warp_prepare_chunk(v0, v1, act + c);
   }
 }
 
 cudaError_t launch_norm_prepare(const float* x, const float* w, uint32_t n, float eps, float* h,
                                 void* act, cudaStream_t stream) {
-  norm_prepare_kernel<<<1, 1024, 0, stream>>>(x, w, n, eps, h, static_cast<ActChunk*>(act));
-  return cudaGetLastError();
+  return launch_k(norm_prepare_kernel, 1, 1024, 0, stream, x, w, n, eps, h,
+                  static_cast<ActChunk*>(act));
 }
 
-// a = silu(gate) * up fused with a's activation preparation (one thread per 64 columns;
-// the plane scales are per 32 columns, so no cross-thread reduction is needed).
+// a = silu(gate) * up fused with a's activation preparation (one warp per 64 columns;
+// the plane scales are per 32 columns, so no cross-warp reduction is needed).
 __global__ void silu_gate_prepare_kernel(const float* __restrict__ gate,
                                          const float* __restrict__ up, uint32_t n, float* a,
                                          ActChunk* act) {
-  const uint32_t c = blockIdx.x * blockDim.x + threadIdx.x;
+  pdl_wait();
+  pdl_trigger();
+  const uint32_t c = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   if (c >= n / 64u) return;
-  float va[32], vb[32];
-#pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    va[i] = silu(gate[64u * c + i]) * up[64u * c + i];
-    vb[i] = silu(gate[64u * c + 32u + i]) * up[64u * c + 32u + i];
-  }
+  const uint32_t i = 64u * c + 2u * (threadIdx.x & 31u);
+  const float v0 = silu(gate[i]) * up[i], v1 = silu(gate[i + 1u]) * up[i + 1u];
   if (a != nullptr) {
-#pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      a[64u * c + i] = va[i];
-      a[64u * c + 32u + i] = vb[i];
-    }
+    a[i] = v0;
+    a[i + 1u] = v1;
   }
-  XChunk xr;
-  quantize_half(va, xr.ah, xr.al, xr.sa, xr.suma, xr.qh[0], xr.ql[0], xr.qh[1], xr.ql[1]);
-  quantize_half(vb, xr.bh, xr.bl, xr.sb, xr.sumb, xr.qh[2], xr.ql[2], xr.qh[3], xr.ql[3]);
-  store_act_chunk(xr, act + c);
+  warp_prepare_chunk(v0, v1, act + c);
 }
 
 cudaError_t launch_silu_gate_prepare(const float* gate, const float* up, uint32_t n, float* a,
                                      void* act, cudaStream_t stream) {
   const uint32_t chunks = n / 64u;
-  silu_gate_prepare_kernel<<<(chunks + 63u) / 64u, 64, 0, stream>>>(gate, up, n, a,
-                                                                    static_cast<ActChunk*>(act));
-  return cudaGetLastError();
+  return launch_k(silu_gate_prepare_kernel, (chunks + 3u) / 4u, 128, 0, stream, gate, up, n, a,
+                  static_cast<ActChunk*>(act));
 }
 
 int device_sm_count() {

@@ -81,10 +81,31 @@ __device__ __forceinline__ void tma_load_1d(void* dst_smem, const void* src_gmem
       : "memory");
 }
 
+// Same without an L2 cache hint.
+__device__ __forceinline__ void tma_load_1d(void* dst_smem, const void* src_gmem, uint32_t bytes,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_addr(dst_smem)),
+      "l"(src_gmem), "r"(bytes), "r"(smem_addr(bar))
+      : "memory");
+}
+
 __device__ __forceinline__ uint64_t l2_evict_first_policy() {
   uint64_t policy;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
   return policy;
+}
+
+// Programmatic dependent launch.  pdl_wait: block until the grids this one depends on
+// have completed and their writes are visible (a no-op without a programmatic edge);
+// every kernel calls it before reading another kernel's output or writing global
+// memory -- only immutable data (the weights) may be read before it.  pdl_trigger:
+// allow the dependent grid to start launching (its CTAs then run their own
+// pre-wait prologue while this grid finishes).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 // IEEE fp16 bit pattern -> fp32 (exact for every finite value; the reference's

@@ -13,6 +13,7 @@
 // 32-value sub-blocks 2*(c%4), 2*(c%4)+1 of block c/4.
 #pragma once
 
+#include "iq_grids.h"
 #include "qg_common.cuh"
 
 namespace qg {
@@ -186,13 +187,19 @@ struct XChunk {
 __device__ __forceinline__ void quantize_half(const float (&v)[32], uint32_t (&hi)[8],
                                               uint32_t (&lo)[8], float& s, float& sum,
                                               int& qh0, int& ql0, int& qh1, int& ql1) {
-  float m = 0.f, t = 0.f;
+  float m = 0.f;
 #pragma unroll
-  for (int j = 0; j < 32; ++j) {
-    m = fmaxf(m, fabsf(v[j]));
-    t += v[j];
+  for (int j = 0; j < 32; ++j) m = fmaxf(m, fabsf(v[j]));
+  // Pairwise-tree sum, the order warp_prepare_chunk's butterfly produces.
+  float p[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) p[j] = v[2 * j] + v[2 * j + 1];
+#pragma unroll
+  for (int len = 8; len >= 1; len >>= 1) {
+#pragma unroll
+    for (int j = 0; j < len; ++j) p[j] = p[2 * j] + p[2 * j + 1];
   }
-  sum = t;
+  sum = p[0];
   s = m > 0.f ? m * (1.0f / 126.0f) : 1.0f;
   const float inv = 1.0f / s;
   // Round to nearest even with the 1.5 * 2^23 magic number: for |u| < 2^22 the low
@@ -509,39 +516,75 @@ __device__ __forceinline__ float chunk_dot<QG_FMT_IQ3S>(const uint8_t* rp, const
   return res;
 }
 
-// Build the IQ tables of a format into shared memory (all threads of the caller).
-__device__ __forceinline__ uint2 sign_bytes(uint32_t s, uint32_t v) {
-  uint32_t lo = 0u, hi = 0u;
-#pragma unroll
-  for (int l = 0; l < 4; ++l) {
-    lo |= ((s >> l) & 1u ? v : 0u) << (8 * l);
-    hi |= ((s >> (l + 4)) & 1u ? v : 0u) << (8 * l);
+// The replicated tables, built at compile time from the codebooks (64 KB per IQ
+// format, in the IqTables layout) and copied into each CTA's shared memory with one
+// bulk copy.
+struct __align__(16) ReplicatedTables {
+  uint32_t w[16384];
+};
+
+namespace tables_detail {
+constexpr uint16_t kIq2Kgrid[1024] = {QG_IQ2S_KGRID_VALUES};
+constexpr uint32_t kIq3Grid[512] = {QG_IQ3S_GRID_VALUES};
+
+constexpr void put_sign_copies(ReplicatedTables& t, uint32_t word_base, uint32_t mag) {
+  for (uint32_t e = 0; e < 256u; ++e) {
+    uint32_t lo = 0u, hi = 0u;
+    for (uint32_t l = 0; l < 4u; ++l) {
+      lo |= (((e >> l) & 1u) ? mag : 0u) << (8u * l);
+      hi |= (((e >> (l + 4u)) & 1u) ? mag : 0u) << (8u * l);
+    }
+    for (uint32_t r = 0; r < 16u; ++r) {
+      t.w[word_base + 2u * ((e << 4) | r)] = lo;
+      t.w[word_base + 2u * ((e << 4) | r) + 1u] = hi;
+    }
   }
-  return make_uint2(lo, hi);
 }
 
+constexpr ReplicatedTables make_iq2s() {
+  ReplicatedTables t{};
+  for (uint32_t e = 0; e < 1024u; ++e) {
+    const uint32_t G = kIq2Kgrid[e];
+    uint32_t lo = 0u, hi = 0u;
+    for (uint32_t l = 0; l < 4u; ++l) {
+      lo |= (((G >> (2u * l)) & 3u) << 1) << (8u * l);
+      hi |= (((G >> (2u * (l + 4u))) & 3u) << 1) << (8u * l);
+    }
+    for (uint32_t r = 0; r < 4u; ++r) {
+      const uint32_t slot = ((e >> 2) << 4) | ((e & 3u) << 2) | r;
+      t.w[2u * slot] = lo;
+      t.w[2u * slot + 1u] = hi;
+    }
+  }
+  put_sign_copies(t, 8192u, 0x0eu);
+  return t;
+}
+
+constexpr ReplicatedTables make_iq3s() {
+  ReplicatedTables t{};
+  for (uint32_t e = 0; e < 512u; ++e) {
+    for (uint32_t r = 0; r < 16u; ++r) t.w[(e << 4) | r] = kIq3Grid[e];
+  }
+  put_sign_copies(t, 8192u, 0x1eu);
+  return t;
+}
+}  // namespace tables_detail
+
+extern __device__ const ReplicatedTables g_iq2s_tables;
+extern __device__ const ReplicatedTables g_iq3s_tables;
+
+template <int FMT>
+__device__ __forceinline__ const ReplicatedTables* replicated_tables() {
+  return FMT == QG_FMT_IQ2S ? &g_iq2s_tables : &g_iq3s_tables;
+}
+
+// All-thread copy of the format's tables into shared memory (fallback kernels).
 template <int FMT>
 __device__ __forceinline__ void build_iq_tables(uint8_t* base, uint32_t tid, uint32_t n) {
-  if (FMT == QG_FMT_IQ2S) {
-    uint2* k2 = reinterpret_cast<uint2*>(base);
-    uint2* s2 = k2 + 4096;
-    for (uint32_t i = tid; i < 4096u; i += n) {
-      const uint32_t e = ((i >> 4) << 2) | ((i >> 2) & 3u);  // inverse of kgrid2_slot
-      const uint32_t G = g_iq2s_kgrid[e];
-      uint32_t lo = 0u, hi = 0u;
-#pragma unroll
-      for (int l = 0; l < 4; ++l) {
-        lo |= (((G >> (2 * l)) & 3u) << 1) << (8 * l);
-        hi |= (((G >> (2 * (l + 4))) & 3u) << 1) << (8 * l);
-      }
-      k2[i] = make_uint2(lo, hi);
-    }
-    for (uint32_t i = tid; i < 4096u; i += n) s2[i] = sign_bytes(i >> 4, 0x0eu);
-  } else if (FMT == QG_FMT_IQ3S) {
-    uint32_t* g3 = reinterpret_cast<uint32_t*>(base);
-    uint2* s3 = reinterpret_cast<uint2*>(base + 32768);
-    for (uint32_t i = tid; i < 8192u; i += n) g3[i] = g_iq3s_grid[i >> 4];
-    for (uint32_t i = tid; i < 4096u; i += n) s3[i] = sign_bytes(i >> 4, 0x1eu);
+  if (FMT == QG_FMT_IQ2S || FMT == QG_FMT_IQ3S) {
+    const uint4* src = reinterpret_cast<const uint4*>(replicated_tables<FMT>());
+    uint4* dst = reinterpret_cast<uint4*>(base);
+    for (uint32_t i = tid; i < 4096u; i += n) dst[i] = __ldg(src + i);
   }
 }
 
@@ -603,6 +646,58 @@ __device__ __forceinline__ void store_act_chunk(const XChunk& x, ActChunk* dst) 
                     __float_as_uint(x.sumb));
   p[9] = make_uint4(x.qh[0], x.qh[1], x.qh[2], x.qh[3]);
   p[10] = make_uint4(x.ql[0], x.ql[1], x.ql[2], x.ql[3]);
+}
+
+// One warp quantizes one 64-column chunk into its ActChunk: lane l holds columns 2l,
+// 2l+1 (half A = lanes 0-15, half B = lanes 16-31).  Same arithmetic as quantize_half
+// (scale = max|x| / 126 per half, magic-number rounding), so a chunk prepared here is
+// bit-identical to one quantized inside the GEMV.
+__device__ __forceinline__ void warp_prepare_chunk(float v0, float v1, ActChunk* dst) {
+  const uint32_t lane = threadIdx.x & 31u;
+  float m = fmaxf(fabsf(v0), fabsf(v1));
+#pragma unroll
+  for (int off = 8; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+  const float s = m > 0.f ? m * (1.0f / 126.0f) : 1.0f;
+  const float inv = 1.0f / s;
+  constexpr float kRound = 12582912.0f;
+  constexpr int kRoundBits = 0x4b400000;
+  int ia[2], ib[2];
+  const float v[2] = {v0, v1};
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const float u = v[k] * inv;
+    const float ur = u + kRound;
+    ia[k] = __float_as_int(ur) - kRoundBits;
+    const float r = (u - (ur - kRound)) * 256.0f;
+    ib[k] = min(max(__float_as_int(r + kRound) - kRoundBits, -127), 127);
+  }
+  // bytes of columns 2l, 2l+1; the even lane of a pair assembles the 4-column word
+  const uint32_t h2 = __byte_perm(ia[0], ia[1], 0x0040), l2 = __byte_perm(ib[0], ib[1], 0x0040);
+  const uint32_t hn = __shfl_down_sync(0xffffffffu, h2, 1), ln = __shfl_down_sync(0xffffffffu, l2, 1);
+  // sums: exact fp32 over the half (tree order), plane sums over 16-column quarters
+  float t = v0 + v1;
+  int qh = ia[0] + ia[1], ql = ib[0] + ib[1];
+#pragma unroll
+  for (int off = 1; off < 8; off <<= 1) {
+    t += __shfl_xor_sync(0xffffffffu, t, off);
+    qh += __shfl_xor_sync(0xffffffffu, qh, off);
+    ql += __shfl_xor_sync(0xffffffffu, ql, off);
+  }
+  t += __shfl_xor_sync(0xffffffffu, t, 8);
+  const uint32_t half = lane >> 4, word = (lane & 15u) >> 1;
+  uint32_t* w = reinterpret_cast<uint32_t*>(dst);
+  if ((lane & 1u) == 0u) {
+    w[half * 16u + word] = __byte_perm(h2, hn, 0x5410);
+    w[half * 16u + 8u + word] = __byte_perm(l2, ln, 0x5410);
+  }
+  if ((lane & 15u) == 0u) {
+    reinterpret_cast<float*>(w)[32u + half] = s;
+    reinterpret_cast<float*>(w)[34u + half] = t;
+  }
+  if ((lane & 7u) == 0u) {
+    w[36u + (lane >> 3)] = static_cast<uint32_t>(qh);
+    w[40u + (lane >> 3)] = static_cast<uint32_t>(ql);
+  }
 }
 
 // This thread's 64 columns of x, quantized to the two byte planes.

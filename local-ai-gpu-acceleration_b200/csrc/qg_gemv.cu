@@ -35,6 +35,8 @@ namespace qg {
 __device__ unsigned int g_error_word = 0u;
 __device__ uint16_t g_iq2s_kgrid[1024] = {QG_IQ2S_KGRID_VALUES};
 __device__ uint32_t g_iq3s_grid[512] = {QG_IQ3S_GRID_VALUES};
+__device__ const ReplicatedTables g_iq2s_tables = tables_detail::make_iq2s();
+__device__ const ReplicatedTables g_iq3s_tables = tables_detail::make_iq3s();
 
 // One weight matrix of a multi-matrix launch (same format and cols): its tiles are
 // [tile_end of the previous segment, tile_end).
@@ -133,6 +135,8 @@ __global__ void __launch_bounds__(512, 1) gemv_staged_kernel(const GemvArgs a) {
 
   const uint32_t tid = threadIdx.x;
   const uint32_t nthreads = blockDim.x;
+  pdl_wait();
+  pdl_trigger();
   const bool valid = tid < a.rpp * a.tpr;
   const uint32_t slot = valid ? tid / a.tpr : 0u;
   const uint32_t c = valid ? tid - slot * a.tpr : 0u;
@@ -245,6 +249,8 @@ __global__ void __launch_bounds__(512, 1) gemv_staged_kernel(const GemvArgs a) {
 template <int FMT>
 __global__ void __launch_bounds__(256) gemv_rowwise_kernel(const GemvArgs a) {
   __shared__ float part[256];
+  pdl_wait();
+  pdl_trigger();
   const uint32_t row = blockIdx.x;
   if (row >= a.rows) return;
   const uint32_t bpr = a.cols >> 8;
@@ -331,11 +337,14 @@ __global__ void __launch_bounds__(544, 1) gemv_tiled_kernel(const GemvArgs a) {
   const uint32_t loads_per_tile = a.passes >> a.stage_shift;
   const uint32_t S = a.stages;
 
+  uint64_t* table_bar = full + 16;
+  constexpr bool kTables = FMT == QG_FMT_IQ2S || FMT == QG_FMT_IQ3S;
   if (tid == 0u) {
     for (uint32_t s = 0; s < S; ++s) {
       mbar_init(&full[s], 1u);
       mbar_init(&empty[s], nconsumers >> 5);
     }
+    mbar_init(table_bar, 1u);
     fence_mbar_init();
   }
   __syncthreads();
@@ -344,6 +353,12 @@ __global__ void __launch_bounds__(544, 1) gemv_tiled_kernel(const GemvArgs a) {
     // Producer warp: one elected lane streams every stage of this CTA's tiles.
     if (lane == 0u) {
       const uint64_t policy = l2_evict_first_policy();
+      if (kTables) {
+        // The codebook tables (64 KB, L2-resident after the first CTA) in one bulk copy.
+        mbar_arrive_expect_tx(table_bar, sizeof(ReplicatedTables));
+        tma_load_1d(smem + a.table_off, replicated_tables<FMT>(), sizeof(ReplicatedTables),
+                    table_bar);
+      }
       bool ok = true;
       uint32_t s = 0, ephase = 0, issued = 0;
       for (uint32_t i = 0; i < n_my && ok; ++i) {
@@ -386,8 +401,9 @@ __global__ void __launch_bounds__(544, 1) gemv_tiled_kernel(const GemvArgs a) {
   const uint32_t row_stride = bpr * PB, meta_stride = bpr * MB;
   const uint32_t Q = a.stage_rows / a.rpp;
 
-  build_iq_tables<FMT>(smem + a.table_off, tid, nconsumers);
   const IqTables tables = iq_tables<FMT>(smem + a.table_off, tid & 31u);
+  pdl_wait();  // x / act / residual / token come from the previous kernel
+  pdl_trigger();
   XChunk xr;
   if (a.xq != nullptr) {
     load_act_chunk(a.xq + c, xr);
@@ -395,10 +411,10 @@ __global__ void __launch_bounds__(544, 1) gemv_tiled_kernel(const GemvArgs a) {
     load_x_chunk(a.x + 64u * c, a.x_vec != 0u, xr);
   }
   const uint32_t tok = (a.kv != nullptr && a.token != nullptr) ? *a.token : 0u;
-  consumer_sync(nconsumers);  // tables visible
+  bool failed = false;
+  if (kTables && !mbar_wait_bounded(table_bar, 0u)) failed = true;
 
   uint32_t s = 0, phase = 0;
-  bool failed = false;
   for (uint32_t i = 0; i < n_my && !failed; ++i) {
     uint32_t row0;
     const GemvSeg& g = a.seg[tile_segment(a, first + i * stride, row0)];
@@ -540,8 +556,7 @@ cudaError_t launch_gemv_fmt(GemvArgs a, cudaStream_t stream) {
   a.tpr = a.cols / 64u;
   a.x_vec = (reinterpret_cast<uintptr_t>(a.x) & 15u) == 0u ? 1u : 0u;
   if (a.cols < 256u || a.tpr > 512u) {
-    gemv_rowwise_kernel<FMT><<<a.rows, 256, 0, stream>>>(a);
-    return cudaGetLastError();
+    return launch_k(gemv_rowwise_kernel<FMT>, a.rows, 256, 0, stream, a);
   }
   const bool aligned = (reinterpret_cast<uintptr_t>(a.payload) & 15u) == 0u &&
                        (MB == 0u || (reinterpret_cast<uintptr_t>(a.meta) & 15u) == 0u);
@@ -556,15 +571,13 @@ cudaError_t launch_gemv_fmt(GemvArgs a, cudaStream_t stream) {
       if (e != cudaSuccess) return e;
       const uint32_t per_sm = resident_ctas(gemv_tiled_kernel<FMT>, plan.threads, plan.smem_bytes);
       const uint32_t grid = std::max(1u, std::min(plan.num_tiles, per_sm * dev.sms));
-      gemv_tiled_kernel<FMT><<<grid, plan.threads, plan.smem_bytes, stream>>>(a);
-      return cudaGetLastError();
+      return launch_k(gemv_tiled_kernel<FMT>, grid, plan.threads, plan.smem_bytes, stream, a);
     }
   }
   // Unaligned packs (or shapes the tiled plan cannot stage): all-thread copies.
   const GemvPlan plan = plan_staged(FMT, a.rows, a.cols, dev.sms);
   if (plan.smem_bytes > static_cast<uint32_t>(dev.max_smem_optin)) {
-    gemv_rowwise_kernel<FMT><<<a.rows, 256, 0, stream>>>(a);
-    return cudaGetLastError();
+    return launch_k(gemv_rowwise_kernel<FMT>, a.rows, 256, 0, stream, a);
   }
   fill_args(a, plan);
   a.tma_ok = 0u;
@@ -572,8 +585,7 @@ cudaError_t launch_gemv_fmt(GemvArgs a, cudaStream_t stream) {
   if (e != cudaSuccess) return e;
   const uint32_t per_sm = resident_ctas(gemv_staged_kernel<FMT>, plan.threads, plan.smem_bytes);
   const uint32_t grid = std::max(1u, std::min(plan.num_tiles, per_sm * dev.sms));
-  gemv_staged_kernel<FMT><<<grid, plan.threads, plan.smem_bytes, stream>>>(a);
-  return cudaGetLastError();
+  return launch_k(gemv_staged_kernel<FMT>, grid, plan.threads, plan.smem_bytes, stream, a);
 }
 
 // Several matrices of one format and width that read the same x, in one launch (the
@@ -624,8 +636,7 @@ cudaError_t launch_multi_fmt(GemvArgs a, uint32_t nseg, const GemvSeg* segs, cud
   if (e != cudaSuccess) return e;
   const uint32_t per_sm = resident_ctas(gemv_tiled_kernel<FMT>, plan.threads, plan.smem_bytes);
   const uint32_t grid = std::max(1u, std::min(tiles, per_sm * dev.sms));
-  gemv_tiled_kernel<FMT><<<grid, plan.threads, plan.smem_bytes, stream>>>(a);
-  return cudaGetLastError();
+  return launch_k(gemv_tiled_kernel<FMT>, grid, plan.threads, plan.smem_bytes, stream, a);
 }
 
 // Threads per CTA: rows-per-pass is the smallest multiple of 32/group (whole warps)

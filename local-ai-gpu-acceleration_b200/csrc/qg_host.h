@@ -1,12 +1,34 @@
 // qg_host.h -- host-side interfaces shared by the library's translation units.
 #pragma once
 
-#include <cuda_runtime_api.h>
+#include <cuda_runtime.h>
 #include <stdint.h>
+
+#include <utility>
 
 #include "../../include/qgemv_b200.h"
 
 namespace qg {
+
+// Every kernel of the library is launched with programmatic stream serialization:
+// it may start while the previous kernel on the stream finishes, and waits
+// (griddepcontrol.wait) before it reads that kernel's output.  Captured into a CUDA
+// graph this becomes a programmatic dependency edge.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                     cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // Launch configuration of the tiled GEMV for one shape (see qg_gemv.cu).
 struct GemvPlan {
