@@ -207,6 +207,62 @@ def measure_slice(device, args) -> dict:
             "weight_bytes": sl.weight_bytes, "GBps": sl.weight_bytes / (us * 1e-6) / 1e9}
 
 
+def measure_decode(device, args, world: int, rank: int) -> dict:
+    """the 80-layer 70B-class mixed-quant decode step (IQ3_S
+    attention, IQ2_S gate/up, Q5_K down, Q4_K vocab head, fp16 KV cache at context
+    4096), tensor-parallel over the job's N GPUs with NCCL, one graph per token."""
+    import torch
+    import torch.distributed as dist
+
+    from qgemv_b200 import decoder
+    from qgemv_b200.slice import StepGraph
+
+    spec = decoder.ModelSpec()
+    w = decoder.synthetic_rank_weights(spec, rank, world, device, seed=1)
+    nid = None
+    if world > 1:
+        obj = [decoder.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        nid = obj[0]
+    dec = decoder.Decoder(spec, w, rank=rank, tp=world, nccl_id=nid, device=device)
+    x = torch.randn(spec.hidden, device=device)
+    pos = spec.ctx_max - 1
+    stream = torch.cuda.Stream(device)
+    stream.wait_stream(torch.cuda.current_stream(device))
+    for _ in range(2):
+        dec.step(x, pos, stream)
+    stream.synchronize()
+    g = StepGraph(stream, lambda: dec.step(x, pos, stream))
+    for _ in range(max(3, args.warmup)):
+        g.launch()
+    stream.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        g.launch()
+    e1.record(stream)
+    stream.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    token = int(dec.token.item())
+    g.close()
+    dec.close()
+    del w
+    torch.cuda.empty_cache()
+    moved = spec.weight_bytes() + spec.kv_bytes_read(spec.ctx_max)
+    return {"workload": "BASELINE config 5: 80-layer 70B-class decode step, ctx 4096, batch 1",
+            "tp": world, "ms_per_token": ms, "tok_per_s": 1000.0 / ms,
+            "weight_bytes": spec.weight_bytes(), "kv_bytes": spec.kv_bytes_read(spec.ctx_max),
+            "GBps_aggregate": moved / (ms * 1e-3) / 1e9, "token": token,
+            "launches_per_token": spec.layers * 10 + 4 + (2 * spec.layers + 1 if world > 1 else 0)}
+
+
 def run_ours(args) -> int:
     import torch
     import torch.distributed as dist
@@ -358,9 +414,12 @@ def run_ours(args) -> int:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t.item())
     e2e_value = world * bytes_per_step * args.steps / (e2e_ms * 1e-3) / 1e9
-    del graphs, step_graph
 
-    slice_stats = measure_slice(device, args)
+    slice_stats = measure_slice(device, args) if not args.only else None
+    launches_per_step = len(mats) + len(xs)
+    del mats, step_graph, graphs
+    torch.cuda.empty_cache()
+    decode_stats = measure_decode(device, args, world, rank) if not args.only else None
     err = ops.get_error()
     if rank == 0:
         cpu = cpu_reference_sample(8, os.cpu_count() or 1) if world == 1 and not args.only else None
@@ -375,11 +434,12 @@ def run_ours(args) -> int:
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
-            "gpu_launches": (len(mats) + len(xs)) * args.steps,
+            "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks.summary(),
             "error_word": err,
             "per_matvec": per,
             "slice": slice_stats,
+            "decode": decode_stats,
         }
         print(json.dumps(line))
     if world > 1:

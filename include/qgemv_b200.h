@@ -309,6 +309,54 @@ cudaError_t qg_graph_end(cudaStream_t stream, qg_graph* out);
 cudaError_t qg_graph_launch(qg_graph graph, cudaStream_t stream);
 cudaError_t qg_graph_destroy(qg_graph graph);
 
+/* ---------------------------------------------------------------------------
+ * Tensor-parallel decode step of a Llama-style mixed-quant model (
+ * no reference counterpart -- the reference is single-GPU with synthetic attention).
+ * One process per GPU.  Rank r of tp_size holds row shards of Wq/Wk/Wv (its
+ * n_q_heads/tp and n_kv_heads/tp heads), Wg/Wu (ffn/tp rows) and the vocab head
+ * (qg_decoder_shard gives its rows and offset), column shards of Wo (its q heads'
+ * columns) and Wd (its ffn/tp columns), and its kv heads' fp16 KV cache
+ * [n_kv_heads/tp][ctx_max][head_dim].  Per layer: rmsnorm -> q,k,v -> RoPE (adjacent
+ * pairs, angle pos * rope_base^(-2i/head_dim)) and cache append at `pos` -> GQA
+ * attention over positions [0, pos] -> Wo -> all-reduce (+x) -> rmsnorm -> gate,up ->
+ * silu(g)*u -> Wd -> all-reduce (+x1); then final rmsnorm, vocab head and the global
+ * argmax (lowest index wins ties) into *token.  head_dim must be 128.  All launches
+ * and NCCL collectives go on the caller's stream (graph-capturable).
+ * ------------------------------------------------------------------------- */
+typedef struct qg_decoder_dims {
+  uint32_t layers, hidden, n_q_heads, n_kv_heads, head_dim, ffn, vocab, ctx_max;
+  float eps, rope_base;
+  int attn_fmt, ffn_fmt, down_fmt, head_fmt;
+  uint32_t tp_rank, tp_size;
+} qg_decoder_dims;
+
+typedef struct qg_decoder_layer {
+  const float* attn_norm;
+  const float* ffn_norm;
+  const uint8_t *wq, *wk, *wv, *wo, *wg, *wu, *wd;
+  const uint8_t *wq_meta, *wk_meta, *wv_meta, *wo_meta, *wg_meta, *wu_meta, *wd_meta;
+  void* k_cache;
+  void* v_cache;
+} qg_decoder_layer;
+
+typedef struct qg_decoder_s* qg_decoder;
+
+/* NCCL unique id (128 bytes) for rank 0 to share with the other ranks. */
+cudaError_t qg_nccl_unique_id(void* id_out);
+cudaError_t qg_decoder_workspace_bytes(const qg_decoder_dims* d, size_t* bytes);
+cudaError_t qg_decoder_shard(const qg_decoder_dims* d, uint32_t* q_rows, uint32_t* kv_rows,
+                             uint32_t* ffn_rows, uint32_t* vocab_rows, uint32_t* vocab_offset);
+/* Collective over the tp_size ranks when tp_size > 1 (NCCL communicator setup). */
+cudaError_t qg_decoder_create(const qg_decoder_dims* d, const qg_decoder_layer* layers,
+                              const float* final_norm, const uint8_t* head,
+                              const uint8_t* head_meta, void* workspace, const void* nccl_id,
+                              qg_decoder* out);
+cudaError_t qg_decoder_step(qg_decoder dec, const float* x, uint32_t pos, uint32_t* token,
+                            cudaStream_t stream);
+/* Device pointers of the last step's final hidden state and this rank's logits. */
+cudaError_t qg_decoder_views(qg_decoder dec, float** hidden, float** logits);
+cudaError_t qg_decoder_destroy(qg_decoder dec);
+
 /* Reads the library's device error word (QG_ERR_* bits) for the current device and
  * clears it.  Synchronizes the device.  Returns the cudaError_t of the read. */
 cudaError_t qg_get_error(uint32_t* error_bits);

@@ -68,6 +68,13 @@ SIGNATURES: dict[str, list] = {
     "qg_graph_end": [P, P],
     "qg_graph_launch": [P, P],
     "qg_graph_destroy": [P],
+    "qg_nccl_unique_id": [P],
+    "qg_decoder_workspace_bytes": [P, P],
+    "qg_decoder_shard": [P, P, P, P, P, P],
+    "qg_decoder_create": [P, P, P, P, P, P, P, P],
+    "qg_decoder_step": [P, P, U32, P, P],
+    "qg_decoder_views": [P, P, P],
+    "qg_decoder_destroy": [P],
 }
 
 _LIB: ctypes.CDLL | None = None

@@ -11,7 +11,7 @@ from pathlib import Path
 PKG_DIR = Path(__file__).resolve().parents[1]          # local-ai-gpu-acceleration_b200/
 CSRC = PKG_DIR / "csrc"
 LIB_PATH = PKG_DIR / "libqgemv_b200.so"
-SOURCES = ["qg_gemv.cu", "qg_aux.cu", "qg_abi.cu", "qg_slice.cu"]
+SOURCES = ["qg_gemv.cu", "qg_aux.cu", "qg_abi.cu", "qg_slice.cu", "qg_attn.cu", "qg_decode.cu"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
@@ -21,6 +21,7 @@ def nvcc_command(out: Path, extra: list[str] | None = None) -> list[str]:
         NVCC, *ARCH, "-lineinfo", "-O3", "-std=c++17", "-rdc=true",
         "-Xcompiler", "-fPIC,-O2", "--expt-relaxed-constexpr",
         "-shared", "-o", str(out), *[str(CSRC / s) for s in SOURCES],
+        "-lnccl",
         *(extra or []),
     ]
 
