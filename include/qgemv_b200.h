@@ -299,6 +299,23 @@ cudaError_t qg_layer_slice_buffers(const qg_layer_slice* s, void* workspace,
 cudaError_t qg_layer_slice_forward(const qg_layer_slice* s, const float* x, float* out,
                                    void* workspace, cudaStream_t stream);
 
+/* Workspace-free form of qg_layer_slice_forward (no reference counterpart: the
+ * reference's runner always owns its device buffers).  For callers that cannot
+ * allocate device memory -- a plugin host that hands over only weights, activations
+ * and a stream; a serving process whose allocator already holds nearly all of HBM;
+ * a decode loop where cudaMalloc/cudaFree would synchronise the device.  The slice's
+ * intermediates live in a library-owned device array of QG_SLICE_STATIC_SCRATCH_BYTES
+ * per device (enough for hidden 8192 / ffn 28672); nothing is allocated or freed.
+ *  - Returns cudaErrorInvalidValue when qg_layer_slice_workspace_bytes(s) exceeds
+ *    QG_SLICE_STATIC_SCRATCH_BYTES (use qg_layer_slice_forward with a workspace).
+ *  - The first call on each device (that device current) looks up the array's device
+ *    address once (cudaGetSymbolAddress); make that first call before any stream capture.
+ *  - One array per device: calls whose work overlaps on a device (different streams
+ *    or host threads) race on it; serialise them on one stream. */
+#define QG_SLICE_STATIC_SCRATCH_BYTES (1u << 20)
+cudaError_t qg_layer_slice_forward_static(const qg_layer_slice* s, const float* x, float* out,
+                                          cudaStream_t stream);
+
 /* Decode-step graphs (runtime/apps/mixed_sequence_benchmark_runner/main.cpp:4801-4823
  * captures, instantiates and uploads one graph, then replays it): everything enqueued
  * on `stream` between qg_graph_begin and qg_graph_end becomes one graph; the handle

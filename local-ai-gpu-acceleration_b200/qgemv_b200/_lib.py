@@ -64,6 +64,7 @@ SIGNATURES: dict[str, list] = {
     "qg_layer_slice_workspace_bytes": [P, P],
     "qg_layer_slice_buffers": [P, P, P],
     "qg_layer_slice_forward": [P, P, P, P, P],
+    "qg_layer_slice_forward_static": [P, P, P, P],
     "qg_graph_begin": [P],
     "qg_graph_end": [P, P],
     "qg_graph_launch": [P, P],

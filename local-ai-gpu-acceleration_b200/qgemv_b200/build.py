@@ -11,7 +11,8 @@ from pathlib import Path
 PKG_DIR = Path(__file__).resolve().parents[1]          # local-ai-gpu-acceleration_b200/
 CSRC = PKG_DIR / "csrc"
 LIB_PATH = PKG_DIR / "libqgemv_b200.so"
-SOURCES = ["qg_gemv.cu", "qg_aux.cu", "qg_abi.cu", "qg_slice.cu", "qg_attn.cu", "qg_decode.cu"]
+SOURCES = ["qg_gemv.cu", "qg_aux.cu", "qg_abi.cu", "qg_slice.cu", "qg_attn.cu", "qg_decode.cu",
+           "qg_noalloc.cu"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
