@@ -207,6 +207,82 @@ def measure_slice(device, args) -> dict:
             "weight_bytes": sl.weight_bytes, "GBps": sl.weight_bytes / (us * 1e-6) / 1e9}
 
 
+BATCHED_FORMATS = [packs.Q4K_RAW, packs.IQ2S]
+BATCHED_SHAPES = [(28672, 8192), (8192, 28672)]
+BATCHED_SIZES = [1, 8, 16, 32]
+
+
+def measure_batched(device, args, peak: float) -> dict:
+    """{Q4_K, IQ2_S} x {28672x8192, 8192x28672} at batch 1, 8, 16, 32.
+    Batch 1 is the GEMV (qg_act_prepare + qg_gemv_act); batch >= 2 is qg_gemm_batched
+    (tensor cores).  Each graph replay walks a rotation of pack copies totalling >= 400 MB,
+    so no call finds its weights in L2; time per call = replay time / copies."""
+    import torch
+
+    from qgemv_b200 import ops
+
+    stream = torch.cuda.Stream(device)
+    cases = []
+    for fmt in BATCHED_FORMATS:
+        for rows, cols in BATCHED_SHAPES:
+            pk = packs.synthetic_pack(fmt, rows, cols, seed=rows ^ cols ^ fmt)
+            nbytes = packs.pack_bytes(fmt, rows, cols)
+            copies = max(2, -(-400_000_000 // nbytes))
+            base = torch.from_numpy(pk.payload).to(device)
+            payloads = [base] + [base.clone() for _ in range(copies - 1)]
+            del pk
+            for batch in BATCHED_SIZES:
+                x = torch.randn(batch, cols, device=device)
+                y = torch.empty(batch, rows, device=device)
+                if batch == 1:
+                    act = torch.empty(ops.act_bytes(cols), dtype=torch.uint8, device=device)
+
+                    def call(p, x=x, y=y, act=act):
+                        ops.act_prepare(x[0], act, stream=stream)
+                        ops.gemv_act(fmt, p, None, x[0], act, rows, cols, y=y[0], stream=stream)
+                    launches = 2
+                else:
+                    ws = torch.empty(ops.gemm_batched_workspace_bytes(fmt, batch, rows, cols),
+                                     dtype=torch.uint8, device=device)
+
+                    def call(p, x=x, y=y, ws=ws, batch=batch):
+                        ops.gemm_batched(fmt, p, None, x, rows, cols, y=y, workspace=ws, stream=stream)
+                    launches = 2
+                with torch.cuda.stream(stream):
+                    for p in payloads:  # eager warm-up: kernel attributes
+                        call(p)
+                stream.synchronize()
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=stream):
+                    for p in payloads:
+                        call(p)
+                for _ in range(max(3, args.warmup)):
+                    g.replay()
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                reps = max(5, args.steps)
+                with torch.cuda.stream(stream):
+                    e0.record(stream)
+                    for _ in range(reps):
+                        g.replay()
+                    e1.record(stream)
+                stream.synchronize()
+                us = e0.elapsed_time(e1) * 1e3 / (reps * copies)
+                gbps = nbytes / (us * 1e-6) / 1e9
+                cases.append({
+                    "fmt": packs.FORMAT_NAMES[fmt], "rows": rows, "cols": cols, "batch": batch,
+                    "path": "gemv" if batch == 1 else "tcgen05", "us": round(us, 2),
+                    "weight_GBps": round(gbps, 1), "frac_hbm": round(gbps / peak, 3),
+                    "TFLOPs": round(2.0 * rows * cols * batch / (us * 1e-6) / 1e12, 2),
+                    "launches": launches,
+                })
+                del g
+            del payloads, base
+            torch.cuda.empty_cache()
+    return {"workload": "BASELINE config 4: {Q4_K, IQ2_S} x {28672x8192, 8192x28672} x batch {1,8,16,32}",
+            "l2": ">= 400 MB of pack copies rotated per replay", "cases": cases}
+
+
 def measure_decode(device, args, world: int, rank: int) -> dict:
     """the 80-layer 70B-class mixed-quant decode step (IQ3_S
     attention, IQ2_S gate/up, Q5_K down, Q4_K vocab head, fp16 KV cache at context
@@ -420,6 +496,7 @@ def run_ours(args) -> int:
     del mats, step_graph, graphs
     torch.cuda.empty_cache()
     decode_stats = measure_decode(device, args, world, rank) if not args.only else None
+    batched_stats = measure_batched(device, args, peak) if not args.only else None
     err = ops.get_error()
     if rank == 0:
         cpu = cpu_reference_sample(8, os.cpu_count() or 1) if world == 1 and not args.only else None
@@ -440,6 +517,7 @@ def run_ours(args) -> int:
             "per_matvec": per,
             "slice": slice_stats,
             "decode": decode_stats,
+            "batched": batched_stats,
         }
         print(json.dumps(line))
     if world > 1:

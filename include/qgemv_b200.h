@@ -259,6 +259,22 @@ cudaError_t qg_argmax_token(const float* values, uint32_t n, uint32_t* token,
                             uint32_t token_offset, uint32_t add_token, uint32_t modulus,
                             cudaStream_t stream);
 
+/* Batched GEMM on the tensor cores (no reference counterpart -- every
+ * reference matvec kernel is batch 1): Y[b, r] = sum_c W[r, c] * X[b, c] for b < batch,
+ * X row-major [batch, cols] fp32, Y row-major [batch, rows] fp32, batch 1..32.
+ * Formats: QG_FMT_Q4K_RAW, QG_FMT_Q5K, QG_FMT_IQ2S, QG_FMT_IQ3S (payload 16-B aligned;
+ * `meta` unused).  Weights are expanded to exact fp16 integer tiles and contracted
+ * with tcgen05.mma (M=128, N=16 or 32) against x scaled by a power of two per batch row
+ * and rounded to fp16; |error| <= 2^-11 * ||w_row||_1 * ||x_b||_inf.  Results are
+ * deterministic.  Three launches on `stream`; `workspace` (256-B aligned, caller-owned) holds the
+ * prepared x and the split-row partial sums: qg_gemm_batched_workspace_bytes, queried
+ * with the device current that will run the call (it depends on the SM count). */
+cudaError_t qg_gemm_batched_workspace_bytes(int fmt, uint32_t batch, uint32_t rows, uint32_t cols,
+                                            size_t* bytes);
+cudaError_t qg_gemm_batched(int fmt, const uint8_t* payload, const uint8_t* meta, const float* x,
+                            float* y, uint32_t batch, uint32_t rows, uint32_t cols, void* workspace,
+                            cudaStream_t stream);
+
 /* ---------------------------------------------------------------------------
  * Mixed-format layer slice (no reference counterpart for the
  * weighted RMSNorm, the SiLU gate or the residual add -- the reference's slice uses

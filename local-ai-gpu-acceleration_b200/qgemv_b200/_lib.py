@@ -63,6 +63,8 @@ SIGNATURES: dict[str, list] = {
     "qg_gemv_plan": [c_int, U32, U32, P, P, P, P],
     "qg_layer_slice_workspace_bytes": [P, P],
     "qg_layer_slice_buffers": [P, P, P],
+    "qg_gemm_batched_workspace_bytes": [c_int, U32, U32, U32, P],
+    "qg_gemm_batched": [c_int, P, P, P, P, U32, U32, U32, P, P],
     "qg_layer_slice_forward": [P, P, P, P, P],
     "qg_layer_slice_forward_static": [P, P, P, P],
     "qg_graph_begin": [P],

@@ -78,6 +78,30 @@ def gemv_batched(fmt: int, payload, meta, x: torch.Tensor, rows: int, cols: int,
     return y
 
 
+def gemm_batched_workspace_bytes(fmt: int, batch: int, rows: int, cols: int) -> int:
+    import ctypes
+
+    n = ctypes.c_size_t(0)
+    check("qg_gemm_batched_workspace_bytes", fmt, batch, rows, cols, ctypes.byref(n))
+    return n.value
+
+
+def gemm_batched(fmt: int, payload, meta, x: torch.Tensor, rows: int, cols: int,
+                 y: torch.Tensor | None = None, workspace: torch.Tensor | None = None,
+                 stream=None) -> torch.Tensor:
+    """Y[b] = W x[b] on the tensor cores (qg_gemm_batched); x is [batch, cols] fp32."""
+    require_cuda()
+    batch = x.shape[0]
+    if y is None:
+        y = torch.empty(batch, rows, dtype=torch.float32, device=x.device)
+    if workspace is None:
+        workspace = torch.empty(gemm_batched_workspace_bytes(fmt, batch, rows, cols),
+                                dtype=torch.uint8, device=x.device)
+    check("qg_gemm_batched", fmt, _ptr(payload), _ptr(meta), _ptr(x), _ptr(y), batch, rows, cols,
+          _ptr(workspace), _stream(stream))
+    return y
+
+
 def decode_stage(fmt: int, payload, meta, x, y, kv, token, rows: int, cols: int,
                  kv_words: int, page_words: int, active_pages: int, stream=None) -> None:
     require_cuda()
