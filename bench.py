@@ -64,6 +64,22 @@ def measured_peak() -> tuple[float, str]:
     return FALLBACK_HBM_GBS, "fallback 6.65 TB/s"
 
 
+def prewarm(fn, sync, seconds: float = 0.6, minimum: int = 3) -> int:
+    """Untimed calls of `fn` for at least `seconds` of wall time (and `minimum` calls),
+    so that SM clocks have ramped up from idle before a timed region; `sync` drains the
+    queue every few calls.  Only for work without collectives (ranks may differ in the
+    number of calls)."""
+    t0 = time.perf_counter()
+    n = 0
+    while n < minimum or time.perf_counter() - t0 < seconds:
+        fn()
+        n += 1
+        if n % 4 == 0:
+            sync()
+    sync()
+    return n
+
+
 class ClockSampler:
     """nvidia-smi sampling of SM clocks / throttle reasons during the timed region."""
 
@@ -192,6 +208,7 @@ def measure_slice(device, args) -> dict:
     g = StepGraph(stream, lambda: sl.forward(x, out, stream))
     for _ in range(max(3, args.warmup)):
         g.launch()
+    prewarm(g.launch, stream.synchronize, seconds=0.4)
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     n = max(20, args.steps * 5)
@@ -247,7 +264,7 @@ def measure_batched(device, args, peak: float) -> dict:
 
                     def call(p, x=x, y=y, ws=ws, batch=batch):
                         ops.gemm_batched(fmt, p, None, x, rows, cols, y=y, workspace=ws, stream=stream)
-                    launches = 2
+                    launches = 3
                 with torch.cuda.stream(stream):
                     for p in payloads:  # eager warm-up: kernel attributes
                         call(p)
@@ -256,8 +273,10 @@ def measure_batched(device, args, peak: float) -> dict:
                 with torch.cuda.graph(g, stream=stream):
                     for p in payloads:
                         call(p)
-                for _ in range(max(3, args.warmup)):
-                    g.replay()
+                with torch.cuda.stream(stream):
+                    for _ in range(max(3, args.warmup)):
+                        g.replay()
+                    prewarm(g.replay, stream.synchronize, seconds=0.3)
                 e0 = torch.cuda.Event(enable_timing=True)
                 e1 = torch.cuda.Event(enable_timing=True)
                 reps = max(5, args.steps)
@@ -309,8 +328,11 @@ def measure_decode(device, args, world: int, rank: int) -> dict:
         dec.step(x, pos, stream)
     stream.synchronize()
     g = StepGraph(stream, lambda: dec.step(x, pos, stream))
-    for _ in range(max(3, args.warmup)):
+    # warm-up: a fixed number of replays on every rank (the graph holds collectives)
+    for i in range(max(3, args.warmup) + 20):
         g.launch()
+        if i % 4 == 3:
+            stream.synchronize()
     stream.synchronize()
     if world > 1:
         dist.barrier()
@@ -409,7 +431,10 @@ def run_ours(args) -> int:
         dist.barrier()
 
     with ClockSampler(local) as clocks:
-        time.sleep(0.4)
+        # keep the GPU busy (untimed) while the sampler starts and the clocks settle
+        prewarm(step_graph.replay, torch.cuda.synchronize, seconds=0.6)
+        if world > 1:
+            dist.barrier()
         t_begin = torch.cuda.Event(enable_timing=True)
         t_end = torch.cuda.Event(enable_timing=True)
         t_begin.record(stream)
@@ -474,7 +499,7 @@ def run_ours(args) -> int:
 
     for _ in range(max(3, args.warmup)):
         e2e_step()
-    torch.cuda.synchronize()
+    prewarm(e2e_step, torch.cuda.synchronize, seconds=0.4)
     if world > 1:
         dist.barrier()
     e0 = torch.cuda.Event(enable_timing=True)
