@@ -1,6 +1,6 @@
 // qg_common.cuh -- device helpers shared by the sm_100a decode kernels.
 //
-//  * 1-D TMA (cp.async.bulk, no multicast) into shared memory with mbarrier
+//  * 1-D TMA (cp.async.bulk, plain form) into shared memory with mbarrier
 //    completion, and bounded mbarrier waits that record QG_ERR_WAIT_TIMEOUT in the
 //    library's error word instead of spinning forever.
 //  * Field decoders for the GGUF super-blocks: fp16 scale words and the 6-bit
@@ -70,7 +70,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
 }
 
 // Global -> shared bulk copy of `bytes` (multiple of 16, both addresses 16-B aligned),
-// completing on `bar`.  Plain (non-multicast) form: the source is this GPU's memory.
+// completing on `bar`.  Plain form: the source is this GPU's own memory.
 // L2 evict-first: weights are streamed once per call.
 __device__ __forceinline__ void tma_load_1d(void* dst_smem, const void* src_gmem, uint32_t bytes,
                                             uint64_t* bar, uint64_t policy) {

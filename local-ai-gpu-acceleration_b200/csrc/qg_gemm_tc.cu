@@ -36,7 +36,7 @@
 //
 // CTA roles (15 warps, one CTA per SM):
 //   warp 0      weight producer: one 2-D tensor copy per unit (cp.async.bulk.tensor, a
-//               box of 128 rows x one block, no multicast) into a raw ring -- or, when
+//               box of 128 rows x one block, plain form) into a raw ring -- or, when
 //               the row stride is not a 16-B multiple, one 1-D bulk copy per row;
 //   warp 1      allocates tensor memory; lane 0 issues the MMAs (M=128, N=16|32, K=16);
 //   warps 2-9   dequantize: warp w handles rows 32*(w%4).. (its tensor-memory lanes)
