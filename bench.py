@@ -224,6 +224,91 @@ def measure_slice(device, args) -> dict:
             "weight_bytes": sl.weight_bytes, "GBps": sl.weight_bytes / (us * 1e-6) / 1e9}
 
 
+REF_LAUNCHERS = {
+    # the reference's launcher per sweep format (decode_kernels.h:345-394,502-513); the
+    # Q4_K one is its fastest raw-block variant, the others take rows_limit = rows
+    packs.Q4K_RAW: ("rtxllm_launch_q4k_matvec_decode_warp_broadcast_vec4x4", False),
+    packs.Q5K: ("rtxllm_launch_q5k_matvec_decode_probe", True),
+    packs.IQ2S: ("rtxllm_launch_iq2s_matvec_decode_probe", True),
+    packs.IQ3S: ("rtxllm_launch_iq3s_matvec_decode_probe", True),
+}
+
+
+def measure_reference_gpu(device, mats, xs, args) -> dict | None:
+    """The reference's own GPU launchers -- runtime/kernels/decode/decode_kernels.cu compiled
+    unmodified for sm_100a into oracle/_ref -- on the sweep's packs, beside this library's
+    launchers of the same names and arguments (logits + token update, no KV pages).  One
+    step = the 16 matrices in sweep order (no L2 reuse between uses of a matrix); per-launch
+    times from event nodes inside one graph per arm, after an untimed warm-up."""
+    import ctypes
+
+    import torch
+
+    from qgemv_b200 import _lib
+
+    path = REPO / "oracle" / "_ref" / "libref_oracle.so"
+    if not path.exists():
+        return None
+    arms = {"reference": ctypes.CDLL(str(path)), "ours": _lib.lib()}
+    P, U = ctypes.c_void_p, ctypes.c_uint32
+    token = torch.zeros(1, dtype=torch.int32, device=device)
+    kv = torch.zeros(64, dtype=torch.float32, device=device)
+    stream = torch.cuda.Stream(device)
+    out = {}
+    for arm, lib in arms.items():
+        fns = {}
+        for fmt, (name, has_limit) in REF_LAUNCHERS.items():
+            fn = getattr(lib, name)
+            fn.restype = ctypes.c_int
+            fn.argtypes = [P, P, P, P, P, U, U] + ([U] if has_limit else []) + [U, U, U, P]
+            fns[fmt] = (fn, has_limit)
+
+        def step(events=None, fns=fns):
+            for i, m in enumerate(mats):
+                fn, has_limit = fns[m["fmt"]]
+                lim = (m["rows"],) if has_limit else ()
+                rc = fn(m["payload"].data_ptr(), xs[m["cols"]].data_ptr(), m["y"].data_ptr(), kv.data_ptr(),
+                        token.data_ptr(), m["rows"], m["cols"], *lim, 0, 0, 0, stream.cuda_stream)
+                if rc != 0:
+                    raise RuntimeError(f"{arm} launcher for format {m['fmt']} returned {rc}")
+                if events is not None:
+                    events[i + 1].record(stream)
+
+        with torch.cuda.stream(stream):
+            step()
+        stream.synchronize()
+        evs = [[torch.cuda.Event(enable_timing=True, external=True) for _ in range(len(mats) + 1)]
+               for _ in range(args.steps)]
+        graphs = []
+        for ev in evs:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                ev[0].record(stream)
+                step(ev)
+            graphs.append(g)
+        with torch.cuda.stream(stream):
+            prewarm(lambda: [g.replay() for g in graphs], stream.synchronize, seconds=0.5, minimum=1)
+            for g in graphs:
+                g.replay()
+        stream.synchronize()
+        out[arm] = [statistics.median(ev[i].elapsed_time(ev[i + 1]) for ev in evs) for i in range(len(mats))]
+        del graphs
+    per = []
+    for i, m in enumerate(mats):
+        r_ms, o_ms = out["reference"][i], out["ours"][i]
+        per.append({"format": packs.FORMAT_NAMES[m["fmt"]], "rows": m["rows"], "cols": m["cols"],
+                    "reference_us": round(r_ms * 1e3, 2), "ours_us": round(o_ms * 1e3, 2),
+                    "speedup": round(r_ms / o_ms, 2)})
+    total_bytes = sum(m["bytes"] for m in mats)
+    ref_ms, our_ms = sum(out["reference"]), sum(out["ours"])
+    return {"kind": "reference GPU kernels (decode_kernels.cu, unmodified, compiled for sm_100a)",
+            "launchers": {packs.FORMAT_NAMES[f]: n for f, (n, _) in REF_LAUNCHERS.items()},
+            "sweep_us_reference": round(ref_ms * 1e3, 1), "sweep_us_ours": round(our_ms * 1e3, 1),
+            "GBps_reference": round(total_bytes / (ref_ms * 1e-3) / 1e9, 1),
+            "GBps_ours": round(total_bytes / (our_ms * 1e-3) / 1e9, 1),
+            "speedup": round(ref_ms / our_ms, 2), "per_matvec": per}
+
+
 BATCHED_FORMATS = [packs.Q4K_RAW, packs.IQ2S]
 BATCHED_SHAPES = [(28672, 8192), (8192, 28672)]
 BATCHED_SIZES = [1, 8, 16, 32]
@@ -516,6 +601,7 @@ def run_ours(args) -> int:
         e2e_ms = float(t.item())
     e2e_value = world * bytes_per_step * args.steps / (e2e_ms * 1e-3) / 1e9
 
+    ref_gpu = measure_reference_gpu(device, mats, xs, args) if world == 1 and not args.only else None
     slice_stats = measure_slice(device, args) if not args.only else None
     launches_per_step = len(mats) + len(xs)
     del mats, step_graph, graphs
@@ -540,6 +626,7 @@ def run_ours(args) -> int:
             "clocks": clocks.summary(),
             "error_word": err,
             "per_matvec": per,
+            "reference_gpu": ref_gpu,
             "slice": slice_stats,
             "decode": decode_stats,
             "batched": batched_stats,

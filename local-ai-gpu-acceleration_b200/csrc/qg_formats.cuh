@@ -308,17 +308,15 @@ __device__ __forceinline__ void q4_nibble_dot(const uint4 q0, const uint4 q1, co
 //    one bank pair per lane of a half-warp -> conflict-free;
 //  * 4 copies of the 8-byte IQ2_S expanded grid: copy r = k % 4 occupies only bank
 //    pairs r, r+4, r+8, r+12, so 4 lanes of a half-warp compete for 4 pairs.
+// The pointers are already offset to this lane's copy, so a lookup is one shifted add:
+// kgrid2[4 e], sign2[16 e], grid3[16 e], sign3[16 e].
 struct IqTables {
-  const uint2* kgrid2;    // IQ2_S: 1024 entries x 4 copies, 8 bytes 2k
-  const uint2* sign2;     // IQ2_S: 256 entries x 16 copies, bytes (sign ? 0x0E : 0)
-  const uint32_t* grid3;  // IQ3_S: 512 entries x 16 copies, 4 magnitudes
-  const uint2* sign3;     // IQ3_S: 256 entries x 16 copies, bytes (sign ? 0x1E : 0)
+  const uint2* kgrid2;    // IQ2_S: 1024 entries x 4 copies (slot 4e + k%4), 8 bytes 2k
+  const uint2* sign2;     // IQ2_S: 256 entries x 16 copies (slot 16e + k), bytes (sign ? 0x0E : 0)
+  const uint32_t* grid3;  // IQ3_S: 512 entries x 16 copies (slot 16e + k), 4 magnitudes
+  const uint2* sign3;     // IQ3_S: 256 entries x 16 copies (slot 16e + k), bytes (sign ? 0x1E : 0)
   uint32_t k;             // lane % 16
 };
-
-__device__ __forceinline__ uint32_t kgrid2_slot(uint32_t e, uint32_t k) {
-  return ((e >> 2) << 4) | ((e & 3u) << 2) | (k & 3u);
-}
 
 template <int FMT>
 __device__ __forceinline__ float chunk_dot(const uint8_t* rp, const uint8_t* rm, uint32_t c,
@@ -456,8 +454,8 @@ __device__ __forceinline__ float chunk_dot<QG_FMT_IQ2S>(const uint8_t* rp, const
 #pragma unroll
     for (int g = 0; g < 4; ++g) {
       const uint32_t idx = byte_of(gl[ib], g) | ((qhb << (8 - 2 * g)) & 0x300u);
-      const uint2 k2 = t.kgrid2[kgrid2_slot(idx, t.k)];
-      const uint2 sm = t.sign2[(byte_of(sg[ib], g) << 4) | t.k];
+      const uint2 k2 = t.kgrid2[idx << 2];
+      const uint2 sm = t.sign2[byte_of(sg[ib], g) << 4];
       const uint32_t u0 = k2.x ^ sm.x ^ 0x09090909u;
       const uint32_t u1 = k2.y ^ sm.y ^ 0x09090909u;
       ih[g >> 1] = dp4a(u1, H[2 * g + 1], dp4a(u0, H[2 * g], ih[g >> 1]));
@@ -496,13 +494,13 @@ __device__ __forceinline__ float chunk_dot<QG_FMT_IQ3S>(const uint8_t* rp, const
     int ih = 0, il = 0;
 #pragma unroll
     for (int g = 0; g < 4; ++g) {
-      const uint2 sm = t.sign3[(byte_of(sg[ib], g) << 4) | t.k];
+      const uint2 sm = t.sign3[byte_of(sg[ib], g) << 4];
 #pragma unroll
       for (int p = 0; p < 2; ++p) {
         const int sel = 2 * g + p;
         const uint32_t qb = byte_of(qs[2 * ib + (sel >> 2)], sel & 3);
         const uint32_t idx = qb | (((qhb >> sel) & 1u) << 8u);
-        const uint32_t u = t.grid3[(idx << 4) | t.k] ^ 0x11111111u ^ (p ? sm.y : sm.x);
+        const uint32_t u = t.grid3[idx << 4] ^ 0x11111111u ^ (p ? sm.y : sm.x);
         ih = dp4a(u, H[sel], ih);
         il = dp4a(u, Lp[sel], il);
       }
@@ -551,7 +549,7 @@ constexpr ReplicatedTables make_iq2s() {
       hi |= (((G >> (2u * (l + 4u))) & 3u) << 1) << (8u * l);
     }
     for (uint32_t r = 0; r < 4u; ++r) {
-      const uint32_t slot = ((e >> 2) << 4) | ((e & 3u) << 2) | r;
+      const uint32_t slot = 4u * e + r;
       t.w[2u * slot] = lo;
       t.w[2u * slot + 1u] = hi;
     }
@@ -593,11 +591,11 @@ __device__ __forceinline__ IqTables iq_tables(const uint8_t* base, uint32_t lane
   IqTables t{};
   t.k = lane & 15u;
   if (FMT == QG_FMT_IQ2S) {
-    t.kgrid2 = reinterpret_cast<const uint2*>(base);
-    t.sign2 = t.kgrid2 + 4096;
+    t.kgrid2 = reinterpret_cast<const uint2*>(base) + (t.k & 3u);
+    t.sign2 = reinterpret_cast<const uint2*>(base) + 4096 + t.k;
   } else if (FMT == QG_FMT_IQ3S) {
-    t.grid3 = reinterpret_cast<const uint32_t*>(base);
-    t.sign3 = reinterpret_cast<const uint2*>(base + 32768);
+    t.grid3 = reinterpret_cast<const uint32_t*>(base) + t.k;
+    t.sign3 = reinterpret_cast<const uint2*>(base + 32768) + t.k;
   }
   return t;
 }

@@ -276,6 +276,26 @@ __device__ __forceinline__ bool tc_spin(uint64_t* bar, uint32_t parity, volatile
   return false;
 }
 
+// Up to three phases at once (b1 may be null): the polls are independent, so their
+// latencies overlap.  Bounded like tc_spin.
+__device__ __forceinline__ bool tc_spin3(uint64_t* b1, uint32_t p1, uint64_t* b2, uint32_t p2, uint64_t* b3,
+                                         uint32_t p3, volatile uint32_t* abort) {
+  bool ok1 = b1 == nullptr, ok2 = false, ok3 = false;
+  for (uint32_t it = 0; it < kMaxSpinPolls; ++it) {
+    const bool r1 = ok1 || mbar_test_wait(b1, p1);
+    const bool r2 = ok2 || mbar_test_wait(b2, p2);
+    const bool r3 = ok3 || mbar_test_wait(b3, p3);
+    ok1 = r1;
+    ok2 = r2;
+    ok3 = r3;
+    if (ok1 && ok2 && ok3) return true;
+    if ((it & 1023u) == 1023u && *abort != 0u) return false;
+  }
+  atomicOr(&g_error_word, QG_ERR_WAIT_TIMEOUT);
+  *abort = 1u;
+  return false;
+}
+
 // The same wait done by lane 0 for the whole warp.
 __device__ __forceinline__ bool tc_wait_warp(uint64_t* bar, uint32_t parity, volatile uint32_t* abort,
                                              uint32_t lane) {
@@ -592,12 +612,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
   constexpr uint32_t kTmemA = tmem_a<NB>();
   uint64_t* raw_full = bars;
   uint64_t* raw_empty = raw_full + S;
-  uint64_t* a_full = raw_empty + S;        // [unit slot][half]
-  uint64_t* a_empty = a_full + 2u * kASlots;
-  uint64_t* x_full = a_empty + 2u * kASlots;
-  uint64_t* x_empty = x_full + kXStages;
-  uint64_t* acc_full = x_empty + kXStages;
-  uint64_t* acc_empty = acc_full + kAccSlots;
+  static_assert(kXStages == kAccSlots, "x stages and accumulator slots share unit_done");
+  uint64_t* a_full = raw_empty + S;        // per A slot: both dequantize halves written
+  uint64_t* a_empty = a_full + kASlots;    // per A slot: its MMAs completed
+  uint64_t* x_full = a_empty + kASlots;
+  uint64_t* unit_done = x_full + kXStages; // per unit ring index: all MMAs of the unit completed
+  uint64_t* acc_empty = unit_done + kXStages;
   uint64_t* done = acc_empty + kAccSlots;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
   volatile uint32_t* abort = tmem_slot + 1;
@@ -613,16 +633,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
       mbar_init(&raw_full[i], 1);
       mbar_init(&raw_empty[i], 8);  // one arrival per dequant warp
     }
-    for (uint32_t i = 0; i < 2u * kASlots; ++i) {
-      mbar_init(&a_full[i], 128);   // every thread of one dequant half
+    for (uint32_t i = 0; i < kASlots; ++i) {
+      mbar_init(&a_full[i], 256);   // every dequantize thread
       mbar_init(&a_empty[i], 1);    // MMA commit
     }
     for (uint32_t i = 0; i < kXStages; ++i) {
       mbar_init(&x_full[i], 1);
-      mbar_init(&x_empty[i], 1);
-    }
-    for (uint32_t i = 0; i < kAccSlots; ++i) {
-      mbar_init(&acc_full[i], 1);
+      mbar_init(&unit_done[i], 1);  // MMA commit: frees the x stage, fills the accumulator
       mbar_init(&acc_empty[i], 4);  // one arrival per epilogue warp
     }
     mbar_init(done, 1);
@@ -724,7 +741,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
     for (uint32_t n = 0; n < n_units; ++n) {
       const uint32_t k = static_cast<uint32_t>((u0 + n) % kb);
       const uint32_t xs = n % kXStages;
-      if (n >= kXStages && !tc_wait_warp(&x_empty[xs], ((n / kXStages) & 1u) ^ 1u, abort, lane)) break;
+      if (n >= kXStages && !tc_wait_warp(&unit_done[xs], ((n / kXStages) & 1u) ^ 1u, abort, lane)) break;
       if (lane == 0u) {
         mbar_arrive_expect_tx(&x_full[xs], L::xrec);
         tma_load_1d(sX + xs * L::xrec, args.xrec + static_cast<uint64_t>(k) * L::xrec, L::xrec, &x_full[xs]);
@@ -746,33 +763,25 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
       constexpr uint32_t idesc = umma_idesc<NB>();
       const uint32_t a2_base = smem_addr(sA2), x_base = smem_addr(sX);
       for (uint32_t n = 0; n < n_units; ++n) {
-        const uint32_t t = n % kAccSlots, xs = n % kXStages, as = n % kASlots;
-        if (n >= kAccSlots && !tc_spin(&acc_empty[t], ((n / kAccSlots) & 1u) ^ 1u, abort)) break;
-        if (!tc_spin(&x_full[xs], (n / kXStages) & 1u, abort)) break;
+        const uint32_t t = n % kAccSlots, as = n % kASlots;
+        // accumulator slot free, x landed, A slot written: three independent polls
+        if (!tc_spin3(n >= kAccSlots ? &acc_empty[t] : nullptr, ((n / kAccSlots) & 1u) ^ 1u, &x_full[t],
+                      (n / kXStages) & 1u, &a_full[as], (n / kASlots) & 1u, abort)) {
+          break;
+        }
         tc_fence_after();
         const uint32_t d_q = tmem + t * 2u * NB, d_m = d_q + NB;
-        const uint32_t xb = x_base + xs * L::xrec;
-        bool ok = true;
-        for (uint32_t h = 0; h < 2u; ++h) {
-          const uint32_t ab = 2u * as + h;
-          if (!tc_spin(&a_full[ab], (n / kASlots) & 1u, abort)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t a_t = tmem + kTmemA + as * 128u + h * 64u;
+        const uint32_t xb = x_base + t * L::xrec;
+        const uint32_t a_t = tmem + kTmemA + as * 128u;
 #pragma unroll
-          for (uint32_t j = 0; j < 8u; ++j) {
-            umma_ts(d_q, a_t + 8u * j, umma_desc(xb + (8u * h + j) * (NB * 32u)), idesc, (h | j) != 0u ? 1u : 0u);
-          }
-          if (F::has_min && h == 1u) {
-            umma_ss(d_m, umma_desc(a2_base + as * kA2Bytes), umma_desc(xb + NB * 512u), idesc, 0u);
-          }
-          umma_commit(&a_empty[ab]);
+        for (uint32_t j = 0; j < 16u; ++j) {
+          umma_ts(d_q, a_t + 8u * j, umma_desc(xb + j * (NB * 32u)), idesc, j != 0u ? 1u : 0u);
         }
-        if (!ok) break;
-        umma_commit(&x_empty[xs]);
-        umma_commit(&acc_full[t]);
+        if constexpr (F::has_min) {
+          umma_ss(d_m, umma_desc(a2_base + as * kA2Bytes), umma_desc(xb + NB * 512u), idesc, 0u);
+        }
+        umma_commit(&a_empty[as]);
+        umma_commit(&unit_done[t]);
       }
       // every MMA issued must have completed before tensor memory is freed
       umma_commit(done);
@@ -788,9 +797,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
       const uint64_t u = u0 + n;
       const uint32_t tile = static_cast<uint32_t>(u / kb), k = static_cast<uint32_t>(u % kb);
       const uint32_t row = tile * kTileM + r;
-      const uint32_t s = n % S, as = n % kASlots, ab = 2u * as + h;
+      const uint32_t s = n % S, as = n % kASlots;
       if (!tc_wait_warp(&raw_full[s], (n / S) & 1u, abort, lane)) break;
-      if (n >= kASlots && !tc_wait_warp(&a_empty[ab], ((n / kASlots) & 1u) ^ 1u, abort, lane)) break;
+      if (n >= kASlots && !tc_wait_warp(&a_empty[as], ((n / kASlots) & 1u) ^ 1u, abort, lane)) break;
       tc_fence_after();
       const uint32_t a_t = tmem + lane_addr + kTmemA + as * 128u + h * 64u;
       uint8_t* A2 = sA2 + as * kA2Bytes;
@@ -803,7 +812,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
       tmem_wait_st();
       if (F::has_min && h == 1u) fence_proxy_async_smem();  // min tile -> tensor core
       tc_fence_before();
-      mbar_arrive(&a_full[ab]);
+      mbar_arrive(&a_full[as]);
       __syncwarp();
       if (lane == 0u) mbar_arrive(&raw_empty[s]);
     }
@@ -829,7 +838,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
         dq = FMT == QG_FMT_IQ2S ? d * 0.125f : d;
         if constexpr (F::has_min) dm = h2f(*reinterpret_cast<const uint16_t*>(blk + 2));
       }
-      if (!tc_wait_warp(&acc_full[t], (n / kAccSlots) & 1u, abort, lane)) break;
+      if (!tc_wait_warp(&unit_done[t], (n / kAccSlots) & 1u, abort, lane)) break;
       tc_fence_after();
       const uint32_t taddr = tmem + ((quarter * 32u) << 16) + t * 2u * NB;
 #pragma unroll
