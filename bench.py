@@ -40,6 +40,10 @@ from qgemv_b200 import packs  # noqa: E402
 SWEEP_FORMATS = [packs.Q4K_RAW, packs.Q5K, packs.IQ2S, packs.IQ3S]
 SWEEP_SHAPES = [(4096, 4096), (14336, 4096), (4096, 14336), (128256, 8192)]
 FALLBACK_HBM_GBS = 6650.0
+# DRAM traffic / algorithmic bytes of the GEMV, per format, from one ncu capture each
+# (dram__bytes_read.sum + dram__bytes_write.sum on 32768 x 8192); the roofline's
+# `traffic` is this ratio times the dominant launch's algorithmic bytes.
+TRAFFIC_RATIO = {packs.IQ3S: 1.026, packs.IQ2S: 1.035}
 METRIC = "weight-stream GB/s, quant matvec sweep (Q4_K/Q5_K/IQ2_S/IQ3_S x 4 shapes, batch 1)"
 CONFIG = {
     "workload": "BASELINE config 2: batch-1 GEMV sweep {Q4_K,Q5_K,IQ2_S,IQ3_S} x "
@@ -560,11 +564,15 @@ def run_ours(args) -> int:
     peak, peak_src = measured_peak()
     dom = max(range(len(mats)), key=lambda i: per[i]["ms"])
     dm = mats[dom]
+    ratio = TRAFFIC_RATIO.get(dm["fmt"])
     roofline = {
         "bound": "hbm", "kernel": f"gemv_tiled_kernel<{packs.FORMAT_NAMES[dm['fmt']]}> {dm['rows']}x{dm['cols']}",
         "achieved": per[dom]["GBps"], "peak": peak, "unit": "GB/s",
         "frac": per[dom]["GBps"] / peak, "peak_source": peak_src,
-        "algorithmic_bytes_per_launch": dm["bytes"], "traffic": None,
+        "algorithmic_bytes_per_launch": dm["bytes"],
+        "traffic": None if ratio is None else round(ratio * dm["bytes"]),
+        "traffic_source": None if ratio is None else
+        "ncu dram__bytes_read.sum + dram__bytes_write.sum of the same kernel at 32768 rows, scaled by rows",
     }
     for row in per:
         row["frac_of_peak"] = row["GBps"] / peak

@@ -38,6 +38,7 @@ def check_rows(port, pk, x, y, rows, cols, r0=0, r1=None):
     (1000, 2048, 17),   # N=32 with padded batch rows, tiles split over 8 CTAs
     (2048, 4096, 32),   # uneven stream-K ranges over all SMs
     (200, 1024, 1),
+    (100, 512, 16),     # fewer rows than one tile: per-row copies instead of the tensor map
 ])
 def test_gemm_batched_vs_oracle(cuda, port, fmt, rows, cols, batch):
     pk = packs.synthetic_pack(fmt, rows, cols, seed=rows * 7 + cols + fmt)
