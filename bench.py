@@ -394,7 +394,10 @@ def measure_batched(device, args, peak: float) -> dict:
 def measure_decode(device, args, world: int, rank: int) -> dict:
     """the 80-layer 70B-class mixed-quant decode step (IQ3_S
     attention, IQ2_S gate/up, Q5_K down, Q4_K vocab head, fp16 KV cache at context
-    4096), tensor-parallel over the job's N GPUs with NCCL, one graph per token."""
+    4096), tensor-parallel over the job's N GPUs, one graph per token.  With N > 1 the
+    step is timed twice on the same weights: the per-layer all-reduces fused into the
+    GEMVs over NVLink peer memory (the reported numbers) and as ncclAllReduce calls
+    between the kernels (`nccl`, the baseline)."""
     import torch
     import torch.distributed as dist
 
@@ -403,51 +406,62 @@ def measure_decode(device, args, world: int, rank: int) -> dict:
 
     spec = decoder.ModelSpec()
     w = decoder.synthetic_rank_weights(spec, rank, world, device, seed=1)
-    nid = None
-    if world > 1:
-        obj = [decoder.nccl_unique_id() if rank == 0 else None]
-        dist.broadcast_object_list(obj, src=0)
-        nid = obj[0]
-    dec = decoder.Decoder(spec, w, rank=rank, tp=world, nccl_id=nid, device=device)
     x = torch.randn(spec.hidden, device=device)
     pos = spec.ctx_max - 1
-    stream = torch.cuda.Stream(device)
-    stream.wait_stream(torch.cuda.current_stream(device))
-    for _ in range(2):
-        dec.step(x, pos, stream)
-    stream.synchronize()
-    g = StepGraph(stream, lambda: dec.step(x, pos, stream))
-    # warm-up: a fixed number of replays on every rank (the graph holds collectives)
-    for i in range(max(3, args.warmup) + 20):
-        g.launch()
-        if i % 4 == 3:
-            stream.synchronize()
-    stream.synchronize()
+
+    def timed(collective: int) -> tuple[float, int]:
+        nid = None
+        if world > 1:
+            obj = [decoder.nccl_unique_id() if rank == 0 else None]
+            dist.broadcast_object_list(obj, src=0)
+            nid = obj[0]
+        dec = decoder.Decoder(spec, w, rank=rank, tp=world, nccl_id=nid, device=device,
+                              collective=collective)
+        stream = torch.cuda.Stream(device)
+        stream.wait_stream(torch.cuda.current_stream(device))
+        for _ in range(2):
+            dec.step(x, pos, stream)
+        stream.synchronize()
+        g = StepGraph(stream, lambda: dec.step(x, pos, stream))
+        # warm-up: a fixed number of replays on every rank (the graph holds collectives)
+        for i in range(max(3, args.warmup) + 20):
+            g.launch()
+            if i % 4 == 3:
+                stream.synchronize()
+        stream.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            g.launch()
+        e1.record(stream)
+        stream.synchronize()
+        ms = e0.elapsed_time(e1) / args.steps
+        if world > 1:
+            t = torch.tensor([ms], dtype=torch.float64, device=device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        token = int(dec.token.item())
+        g.close()
+        dec.close()
+        return ms, token
+
+    ms, token = timed(decoder.COLLECTIVE_NVLINK)
+    nccl = None
     if world > 1:
-        dist.barrier()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(args.steps):
-        g.launch()
-    e1.record(stream)
-    stream.synchronize()
-    ms = e0.elapsed_time(e1) / args.steps
-    if world > 1:
-        t = torch.tensor([ms], dtype=torch.float64, device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    token = int(dec.token.item())
-    g.close()
-    dec.close()
+        ms_n, token_n = timed(decoder.COLLECTIVE_NCCL)
+        nccl = {"ms_per_token": ms_n, "tok_per_s": 1000.0 / ms_n, "token": token_n}
     del w
     torch.cuda.empty_cache()
     moved = spec.weight_bytes() + spec.kv_bytes_read(spec.ctx_max)
     return {"workload": "BASELINE config 5: 80-layer 70B-class decode step, ctx 4096, batch 1",
             "tp": world, "ms_per_token": ms, "tok_per_s": 1000.0 / ms,
+            "collective": "fused NVLink exchange in the Wo/Wd GEMVs" if world > 1 else None,
             "weight_bytes": spec.weight_bytes(), "kv_bytes": spec.kv_bytes_read(spec.ctx_max),
             "GBps_aggregate": moved / (ms * 1e-3) / 1e9, "token": token,
-            "launches_per_token": spec.layers * 10 + 4 + (2 * spec.layers + 1 if world > 1 else 0)}
+            "launches_per_token": spec.layers * 10 + 4, "nccl": nccl}
 
 
 def run_ours(args) -> int:

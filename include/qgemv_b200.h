@@ -353,14 +353,19 @@ cudaError_t qg_graph_destroy(qg_graph graph);
  * pairs, angle pos * rope_base^(-2i/head_dim)) and cache append at `pos` -> GQA
  * attention over positions [0, pos] -> Wo -> all-reduce (+x) -> rmsnorm -> gate,up ->
  * silu(g)*u -> Wd -> all-reduce (+x1); then final rmsnorm, vocab head and the global
- * argmax (lowest index wins ties) into *token.  head_dim must be 128.  All launches
- * and NCCL collectives go on the caller's stream (graph-capturable).
+ * argmax (lowest index wins ties) into *token.  head_dim must be 128.  With
+ * collective = 0 the all-reduces are fused into the Wo/Wd GEMVs and the following
+ * RMSNorm over NVLink peer memory (qg_decoder_create allocates and maps the exchange
+ * buffers, up to 8 ranks).  All launches and NCCL collectives go on the caller's stream
+ * (graph-capturable).
  * ------------------------------------------------------------------------- */
 typedef struct qg_decoder_dims {
   uint32_t layers, hidden, n_q_heads, n_kv_heads, head_dim, ffn, vocab, ctx_max;
   float eps, rope_base;
   int attn_fmt, ffn_fmt, down_fmt, head_fmt;
   uint32_t tp_rank, tp_size;
+  uint32_t collective;  /* tp_size > 1: 0 = all-reduces fused into the GEMVs over NVLink peer
+                           memory (CUDA IPC), 1 = ncclAllReduce between the kernels */
 } qg_decoder_dims;
 
 typedef struct qg_decoder_layer {

@@ -269,6 +269,74 @@ cudaError_t launch_norm_prepare(const float* x, const float* w, uint32_t n, floa
                   static_cast<ActChunk*>(act));
 }
 
+// Gather of a tensor-parallel exchange + RMSNorm + int8 planes (one CTA).  Every word of
+// every rank's slot carries the epoch it was written for: each is re-read (bounded)
+// until it is current, the ranks are summed in rank order (every rank computes the same
+// bits), x_out is written, the epoch advances, and the vector is normalised exactly like
+// norm_prepare_kernel.
+constexpr uint32_t kMaxWordPolls = 1u << 20;  // per word, with 32 ns sleeps after the first few
+
+__global__ void __launch_bounds__(1024) gather_norm_prepare_kernel(
+    const uint64_t* buf, uint32_t* epoch, uint32_t nsrc, uint32_t stride,
+    const float* __restrict__ w, uint32_t n, float eps, float* x_out, float* h, ActChunk* act) {
+  __shared__ float ws[32];
+  __shared__ uint32_t gave_up;
+  pdl_wait();
+  pdl_trigger();
+  const uint32_t E = *epoch + 1u;
+  const uint64_t* base = buf + (E & 1u) * static_cast<size_t>(stride);
+  if (threadIdx.x == 0u) gave_up = 0u;
+  __syncthreads();
+  if (threadIdx.x == 0u) *epoch = E;
+  float sq = 0.f;
+  for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
+    float v = 0.f;
+    for (uint32_t s = 0; s < nsrc; ++s) {
+      const uint64_t* p = base + static_cast<size_t>(s) * n + i;
+      uint64_t word = ld_relaxed_sys_u64(p);
+      for (uint32_t it = 0; static_cast<uint32_t>(word >> 32) != E; ++it) {
+        if (it == kMaxWordPolls || *reinterpret_cast<volatile uint32_t*>(&gave_up) != 0u) {
+          if (atomicExch(&gave_up, 1u) == 0u) atomicOr(&g_error_word, QG_ERR_WAIT_TIMEOUT);
+          break;
+        }
+        if (it > 8u) __nanosleep(32);
+        word = ld_relaxed_sys_u64(p);
+      }
+      v += __uint_as_float(static_cast<uint32_t>(word));
+    }
+    x_out[i] = v;
+    sq += v * v;
+  }
+  for (int off = 16; off > 0; off >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, off);
+  if ((threadIdx.x & 31u) == 0u) ws[threadIdx.x >> 5] = sq;
+  __syncthreads();
+  if (threadIdx.x < 32u) {
+    sq = threadIdx.x < (blockDim.x >> 5) ? ws[threadIdx.x] : 0.f;
+    for (int off = 16; off > 0; off >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, off);
+    if (threadIdx.x == 0u) ws[0] = sq;
+  }
+  __syncthreads();
+  const float inv = 1.0f / sqrtf(ws[0] / static_cast<float>(n) + eps);
+  const uint32_t lane = threadIdx.x & 31u;
+  for (uint32_t c = threadIdx.x >> 5; c < n / 64u; c += blockDim.x >> 5) {
+    const uint32_t i = 64u * c + 2u * lane;
+    const float v0 = x_out[i] * inv * w[i], v1 = x_out[i + 1u] * inv * w[i + 1u];
+    if (h != nullptr) {
+      h[i] = v0;
+      h[i + 1u] = v1;
+    }
+    warp_prepare_chunk(v0, v1, act + c);
+  }
+}
+
+cudaError_t launch_gather_norm_prepare(const uint64_t* buf, uint32_t* epoch, uint32_t nsrc,
+                                       uint32_t stride, const float* w, uint32_t n, float eps,
+                                       float* x_out, float* h, void* act, cudaStream_t stream) {
+  if (nsrc == 0u || nsrc > 32u) return cudaErrorInvalidValue;
+  return launch_k(gather_norm_prepare_kernel, 1, 1024, 0, stream, buf, epoch, nsrc, stride, w, n,
+                  eps, x_out, h, static_cast<ActChunk*>(act));
+}
+
 // a = silu(gate) * up fused with a's activation preparation (one warp per 64 columns;
 // the plane scales are per 32 columns, so no cross-warp reduction is needed).
 __global__ void silu_gate_prepare_kernel(const float* __restrict__ gate,

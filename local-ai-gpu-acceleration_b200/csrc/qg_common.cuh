@@ -108,6 +108,17 @@ __device__ __forceinline__ void pdl_trigger() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// System-scope relaxed 64-bit store / load (single-copy atomic when 8-B aligned): words
+// exchanged with other GPUs over NVLink, each carrying its own epoch.
+__device__ __forceinline__ void st_relaxed_sys_u64(uint64_t* p, uint64_t v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_relaxed_sys_u64(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
 // IEEE fp16 bit pattern -> fp32 (exact for every finite value; the reference's
 // fp16_bits_to_float, decode_kernels.cu:1665-1676, gives the same value).
 __device__ __forceinline__ float h2f(uint32_t bits16) {

@@ -11,8 +11,18 @@
 //   -> rmsnorm*w_ffn -> gate,up (one launch) -> silu(g)*u -> Wd (partial; rank 0 adds
 //   the residual) -> all-reduce.  After the last layer: final rmsnorm -> vocab-shard GEMV
 //   -> shard argmax -> all-gather of (value, index) -> token.
-// Every launch and collective goes on the caller's stream, so one decode step can be
-// captured into one CUDA graph (qg_graph_begin / qg_graph_end).
+// The two all-reduces per layer are fused into the kernels around them, over NVLink
+// peer memory: the Wo / Wd GEMV stores every output row straight into each rank's
+// exchange buffer (this rank's slot) as 64-bit words that carry the exchange's epoch;
+// the next kernel (RMSNorm + int8 planes, which reads the whole vector anyway) reads
+// every rank's slot until each word is current, sums the ranks in rank order and
+// normalises.  No extra launch, fence, flag or collective library call on the hot path;
+// buffers are double-buffered by epoch parity, so a rank can run at most one exchange
+// ahead of the slowest one.  The
+// exchange buffers are allocated by qg_decoder_create and shared through CUDA IPC
+// (handles gathered with NCCL once).  NCCL carries only the token's all-gather.
+// Every launch goes on the caller's stream, so one decode step can be captured into one
+// CUDA graph (qg_graph_begin / qg_graph_end).
 #include <nccl.h>
 
 #include <cstring>
@@ -64,6 +74,9 @@ bool dims_ok(const qg_decoder_dims* d) {
   if (d->n_q_heads % d->tp_size != 0u || d->n_kv_heads % d->tp_size != 0u) return false;
   if (d->n_q_heads / d->n_kv_heads > 16u) return false;
   if (d->ffn % d->tp_size != 0u || d->vocab < d->tp_size || d->ctx_max == 0u) return false;
+  if (d->collective > 1u || (d->tp_size > 1u && d->collective == 0u && d->tp_size > qg::kMaxExchangeRanks)) {
+    return false;
+  }
   const Shape s = shard_shape(d);
   auto width_ok = [](uint32_t n) { return n != 0u && n % 256u == 0u && n / 64u <= 512u; };
   if (!width_ok(d->hidden) || !width_ok(s.q_local) || !width_ok(s.ffn_local)) return false;
@@ -117,6 +130,11 @@ cudaError_t nccl_status(ncclResult_t r) {
 
 }  // namespace
 
+// Exchange region of one rank (cudaMalloc, shared through CUDA IPC): the local epoch,
+// then [2 parities][ranks][hidden] 64-bit words (epoch << 32 | value bits).
+constexpr size_t kExHeader = 256;
+constexpr size_t kExEpoch = 0;  // byte offset inside the header
+
 struct qg_decoder_s {
   qg_decoder_dims dims{};
   Shape shape{};
@@ -128,7 +146,78 @@ struct qg_decoder_s {
   uint8_t* ws = nullptr;
   ncclComm_t comm = nullptr;
   uint32_t last_output = 0;  // workspace offset of the last step's final hidden state
+  uint8_t* ex_local = nullptr;                   // this rank's exchange region
+  uint8_t* ex_peer[qg::kMaxExchangeRanks] = {};  // every rank's region (self included)
 };
+
+namespace {
+
+// Allocates this rank's exchange region, gathers every rank's IPC handle through NCCL
+// and maps the peers' regions.  The handle all-gather also orders every rank's zeroing
+// of its region before any peer can write into it.
+cudaError_t exchange_setup(qg_decoder_s* dec) {
+  const uint32_t n = dec->dims.tp_size, r = dec->dims.tp_rank;
+  const size_t bytes = kExHeader + 2ull * n * dec->dims.hidden * sizeof(uint64_t);
+  cudaError_t e = cudaMalloc(&dec->ex_local, bytes);
+  if (e != cudaSuccess) return e;
+  e = cudaMemset(dec->ex_local, 0, bytes);
+  if (e != cudaSuccess) return e;
+  cudaIpcMemHandle_t mine;
+  e = cudaIpcGetMemHandle(&mine, dec->ex_local);
+  if (e != cudaSuccess) return e;
+  uint8_t* handles = nullptr;
+  e = cudaMalloc(&handles, n * sizeof(cudaIpcMemHandle_t));
+  if (e != cudaSuccess) return e;
+  std::vector<cudaIpcMemHandle_t> all(n);
+  e = cudaMemcpy(handles + r * sizeof(mine), &mine, sizeof(mine), cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) {
+    e = nccl_status(ncclAllGather(handles + r * sizeof(mine), handles, sizeof(mine), ncclUint8,
+                                  dec->comm, nullptr));
+  }
+  if (e == cudaSuccess) e = cudaStreamSynchronize(nullptr);
+  if (e == cudaSuccess) {
+    e = cudaMemcpy(all.data(), handles, n * sizeof(cudaIpcMemHandle_t), cudaMemcpyDeviceToHost);
+  }
+  cudaFree(handles);
+  if (e != cudaSuccess) return e;
+  for (uint32_t p = 0; p < n; ++p) {
+    if (p == r) {
+      dec->ex_peer[p] = dec->ex_local;
+      continue;
+    }
+    void* ptr = nullptr;
+    e = cudaIpcOpenMemHandle(&ptr, all[p], cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) return e;
+    dec->ex_peer[p] = static_cast<uint8_t*>(ptr);
+  }
+  return cudaSuccess;
+}
+
+void exchange_teardown(qg_decoder_s* dec) {
+  for (uint32_t p = 0; p < qg::kMaxExchangeRanks; ++p) {
+    if (dec->ex_peer[p] != nullptr && dec->ex_peer[p] != dec->ex_local) {
+      cudaIpcCloseMemHandle(dec->ex_peer[p]);
+    }
+    dec->ex_peer[p] = nullptr;
+  }
+  if (dec->ex_local != nullptr) cudaFree(dec->ex_local);
+  dec->ex_local = nullptr;
+}
+
+// The Wo / Wd GEMV side of an exchange.
+qg::GemvExchange exchange_out(const qg_decoder_s* dec) {
+  qg::GemvExchange ex{};
+  const uint32_t n = dec->dims.tp_size, r = dec->dims.tp_rank, hid = dec->dims.hidden;
+  ex.n = n;
+  ex.stride = n * hid;
+  for (uint32_t p = 0; p < n; ++p) {
+    ex.out[p] = reinterpret_cast<uint64_t*>(dec->ex_peer[p] + kExHeader) + static_cast<size_t>(r) * hid;
+  }
+  ex.epoch = reinterpret_cast<const uint32_t*>(dec->ex_local + kExEpoch);
+  return ex;
+}
+
+}  // namespace
 
 extern "C" {
 
@@ -188,6 +277,13 @@ cudaError_t qg_decoder_create(const qg_decoder_dims* d, const qg_decoder_layer* 
       delete dec;
       return cudaErrorUnknown;
     }
+    const cudaError_t e = d->collective == 0u ? exchange_setup(dec) : cudaSuccess;
+    if (e != cudaSuccess) {
+      exchange_teardown(dec);
+      ncclCommDestroy(dec->comm);
+      delete dec;
+      return e;
+    }
   }
   *out = dec;
   return cudaSuccess;
@@ -196,6 +292,7 @@ cudaError_t qg_decoder_create(const qg_decoder_dims* d, const qg_decoder_layer* 
 cudaError_t qg_decoder_destroy(qg_decoder dec) {
   if (dec == nullptr) return cudaSuccess;
   cudaError_t e = cudaSuccess;
+  exchange_teardown(dec);
   if (dec->comm != nullptr) e = nccl_status(ncclCommDestroy(dec->comm));
   delete dec;
   return e;
@@ -231,11 +328,42 @@ cudaError_t qg_decoder_step(qg_decoder dec, const float* x, uint32_t pos, uint32
   } while (0)
   const float* cur = x;
   size_t out_off = L.xa;
+  // With tensor parallelism each layer's output stays in the exchange buffers until the
+  // next RMSNorm gathers it (pending); the gather writes the summed vector to its x_out.
+  bool pending = false;
+  const bool fused = tp && d.collective == 0u;
+  const qg::GemvExchange ex = fused ? exchange_out(dec) : qg::GemvExchange{};
+  const uint64_t* ex_buf = fused ? reinterpret_cast<const uint64_t*>(dec->ex_local + kExHeader) : nullptr;
+  uint32_t* ex_epoch = fused ? reinterpret_cast<uint32_t*>(dec->ex_local + kExEpoch) : nullptr;
+  auto norm = [&](const float* src, float* gathered, const float* weight) -> cudaError_t {
+    if (pending) {
+      pending = false;
+      return qg::launch_gather_norm_prepare(ex_buf, ex_epoch, d.tp_size, ex.stride, weight, d.hidden,
+                                            d.eps, gathered, h, w + L.act_x, stream);
+    }
+    return qg::launch_norm_prepare(src, weight, d.hidden, d.eps, h, w + L.act_x, stream);
+  };
+  auto project_out = [&](int fmt, const uint8_t* wt, const uint8_t* wm, const float* in,
+                         const void* act, float* dst, const float* residual,
+                         uint32_t cols) -> cudaError_t {
+    if (fused) {
+      pending = true;
+      return qg::launch_gemv_exchange(fmt, wt, wm, in, act, opart, residual, d.hidden, cols, ex,
+                                      stream);
+    }
+    const cudaError_t e = qg::launch_gemv(fmt, wt, wm, in, act, tp ? opart : dst, residual, nullptr,
+                                          nullptr, 0u, 0u, 0u, d.hidden, cols, stream);
+    if (e != cudaSuccess || !tp) return e;
+    return nccl_status(ncclAllReduce(opart, dst, d.hidden, ncclFloat, ncclSum, dec->comm, stream));
+  };
   for (uint32_t l = 0; l < d.layers; ++l) {
     const qg_decoder_layer& W = dec->layers[l];
     float* x2 = F(out_off);
-    // attention block
-    QG_TRY(qg::launch_norm_prepare(cur, W.attn_norm, d.hidden, d.eps, h, w + L.act_x, stream));
+    // attention block (the previous layer's exchange is gathered into x_in)
+    float* x_in = F(out_off == L.xa ? L.xb : L.xa);
+    const bool gathered = pending;
+    QG_TRY(norm(cur, x_in, W.attn_norm));
+    if (gathered) cur = x_in;
     {
       const uint8_t* p[3] = {W.wq, W.wk, W.wv};
       const uint8_t* m[3] = {W.wq_meta, W.wk_meta, W.wv_meta};
@@ -247,14 +375,10 @@ cudaError_t qg_decoder_step(qg_decoder dec, const float* x, uint32_t pos, uint32
                                   d.ctx_max, pos, d.rope_base, stream));
     QG_TRY(qg::launch_attention(q, W.k_cache, W.v_cache, s.nq_local, s.nkv_local, d.ctx_max,
                                 pos + 1u, F(L.partial), attn, w + L.act_attn, stream));
-    QG_TRY(qg::launch_gemv(d.attn_fmt, W.wo, W.wo_meta, attn, w + L.act_attn, tp ? opart : x1,
-                           rank0 ? cur : nullptr, nullptr, nullptr, 0u, 0u, 0u, d.hidden,
-                           s.q_local, stream));
-    if (tp) {
-      QG_TRY(nccl_status(ncclAllReduce(opart, x1, d.hidden, ncclFloat, ncclSum, dec->comm, stream)));
-    }
-    // feed-forward block
-    QG_TRY(qg::launch_norm_prepare(x1, W.ffn_norm, d.hidden, d.eps, h, w + L.act_x, stream));
+    QG_TRY(project_out(d.attn_fmt, W.wo, W.wo_meta, attn, w + L.act_attn, x1, rank0 ? cur : nullptr,
+                       s.q_local));
+    // feed-forward block (the exchange of Wo is gathered into x1)
+    QG_TRY(norm(x1, x1, W.ffn_norm));
     {
       const uint8_t* p[2] = {W.wg, W.wu};
       const uint8_t* m[2] = {W.wg_meta, W.wu_meta};
@@ -263,18 +387,21 @@ cudaError_t qg_decoder_step(qg_decoder dec, const float* x, uint32_t pos, uint32
       QG_TRY(qg::launch_gemv_multi(d.ffn_fmt, 2, p, m, y, r, d.hidden, h, w + L.act_x, stream));
     }
     QG_TRY(qg::launch_silu_gate_prepare(g, u, s.ffn_local, a, w + L.act_a, stream));
-    QG_TRY(qg::launch_gemv(d.down_fmt, W.wd, W.wd_meta, a, w + L.act_a, tp ? opart : x2,
-                           rank0 ? x1 : nullptr, nullptr, nullptr, 0u, 0u, 0u, d.hidden,
-                           s.ffn_local, stream));
-    if (tp) {
-      QG_TRY(nccl_status(ncclAllReduce(opart, x2, d.hidden, ncclFloat, ncclSum, dec->comm, stream)));
-    }
+    QG_TRY(project_out(d.down_fmt, W.wd, W.wd_meta, a, w + L.act_a, x2, rank0 ? x1 : nullptr,
+                       s.ffn_local));
     cur = x2;
     out_off = (out_off == L.xa) ? L.xb : L.xa;
   }
+  // vocab head (with tensor parallelism the final norm gathers the last layer's output
+  // into the residual buffer the next layer would have used)
+  if (pending) {
+    float* xf = F(out_off == L.xa ? L.xb : L.xa);
+    QG_TRY(norm(cur, xf, dec->final_norm));
+    cur = xf;
+  } else {
+    QG_TRY(norm(cur, nullptr, dec->final_norm));
+  }
   dec->last_output = static_cast<uint32_t>(reinterpret_cast<const uint8_t*>(cur) - w);
-  // vocab head
-  QG_TRY(qg::launch_norm_prepare(cur, dec->final_norm, d.hidden, d.eps, h, w + L.act_x, stream));
   QG_TRY(qg::launch_gemv(d.head_fmt, dec->head, dec->head_meta, h, w + L.act_x, F(L.logits),
                          nullptr, nullptr, nullptr, 0u, 0u, 0u, s.vocab_local, d.hidden, stream));
   uint32_t* cand = reinterpret_cast<uint32_t*>(w + L.cand);

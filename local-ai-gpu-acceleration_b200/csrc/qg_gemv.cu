@@ -82,6 +82,7 @@ struct GemvArgs {
   const ActChunk* xq;     // prepared activation (qg_act_prepare), or null: quantize x here
   GemvSeg seg[kMaxSegs];  // tiled kernel: the matrices of this launch (seg[0] = payload/meta/y)
   uint32_t nseg;
+  GemvExchange ex;        // tiled kernel: optional tensor-parallel exchange of the rows
 };
 
 // Segment of tile `tile` and the tile's first row inside that segment.
@@ -411,6 +412,9 @@ __global__ void __launch_bounds__(544, 1) gemv_tiled_kernel(const GemvArgs a) {
     load_x_chunk(a.x + 64u * c, a.x_vec != 0u, xr);
   }
   const uint32_t tok = (a.kv != nullptr && a.token != nullptr) ? *a.token : 0u;
+  // exchange epoch of this launch and the parity half of the ranks' buffers it fills
+  const uint32_t ex_epoch = a.ex.n != 0u ? *a.ex.epoch + 1u : 0u;
+  const uint32_t ex_off = (ex_epoch & 1u) * a.ex.stride;
   bool failed = false;
   if (kTables && !mbar_wait_bounded(table_bar, 0u)) failed = true;
 
@@ -451,6 +455,10 @@ __global__ void __launch_bounds__(544, 1) gemv_tiled_kernel(const GemvArgs a) {
       const uint32_t row = row0 + t;
       if (a.residual != nullptr) v += a.residual[row];
       g.y[row] = v;
+      if (a.ex.n != 0u) {  // NVLink peer stores of (epoch, value)
+        const uint64_t word = (static_cast<uint64_t>(ex_epoch) << 32) | __float_as_uint(v);
+        for (uint32_t p = 0; p < a.ex.n; ++p) st_relaxed_sys_u64(a.ex.out[p] + ex_off + row, word);
+      }
       if (a.kv != nullptr && row < a.active_pages && a.kv_words > 0u && a.page_words > 0u) {
         const uint64_t kb = static_cast<uint64_t>(row) * a.page_words;
         const uint64_t ko = (tok + row) % a.page_words;
@@ -764,6 +772,62 @@ cudaError_t launch_gemv(int fmt, const uint8_t* payload, const uint8_t* meta, co
     case QG_FMT_Q5K: return launch_gemv_fmt<QG_FMT_Q5K>(a, stream);
     case QG_FMT_IQ2S: return launch_gemv_fmt<QG_FMT_IQ2S>(a, stream);
     case QG_FMT_IQ3S: return launch_gemv_fmt<QG_FMT_IQ3S>(a, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+namespace {
+template <int FMT>
+cudaError_t launch_exchange_fmt(GemvArgs a, cudaStream_t stream) {
+  constexpr uint32_t MB = FmtTraits<FMT>::meta_bytes;
+  const DeviceInfo dev = device_info();
+  a.tpr = a.cols / 64u;
+  a.x_vec = (reinterpret_cast<uintptr_t>(a.x) & 15u) == 0u ? 1u : 0u;
+  const bool aligned = (reinterpret_cast<uintptr_t>(a.payload) & 15u) == 0u &&
+                       (MB == 0u || (reinterpret_cast<uintptr_t>(a.meta) & 15u) == 0u);
+  if (a.cols < 256u || a.tpr > 512u || !aligned) return cudaErrorNotSupported;
+  const GemvPlan plan = plan_gemv(FMT, a.rows, a.cols, dev.sms);
+  if (!plan.tiled || plan.smem_bytes > static_cast<uint32_t>(dev.max_smem_optin)) {
+    return cudaErrorNotSupported;
+  }
+  fill_args(a, plan);
+  a.tma_ok = 1u;
+  a.nseg = 1u;
+  a.seg[0] = GemvSeg{a.payload, a.meta, a.y, a.rows, plan.num_tiles};
+  const cudaError_t e = ensure_smem_attr(gemv_tiled_kernel<FMT>, dev.max_smem_optin);
+  if (e != cudaSuccess) return e;
+  const uint32_t per_sm = resident_ctas(gemv_tiled_kernel<FMT>, plan.threads, plan.smem_bytes);
+  const uint32_t grid = std::max(1u, std::min(plan.num_tiles, per_sm * dev.sms));
+  return launch_k(gemv_tiled_kernel<FMT>, grid, plan.threads, plan.smem_bytes, stream, a);
+}
+}  // namespace
+
+cudaError_t launch_gemv_exchange(int fmt, const uint8_t* payload, const uint8_t* meta,
+                                 const float* x, const void* act, float* y, const float* residual,
+                                 uint32_t rows, uint32_t cols, const GemvExchange& ex,
+                                 cudaStream_t stream) {
+  if (ex.n == 0u || ex.n > kMaxExchangeRanks || ex.epoch == nullptr) {
+    return cudaErrorInvalidValue;
+  }
+  GemvArgs a{};
+  a.payload = payload;
+  a.meta = meta;
+  a.x = x;
+  a.xq = static_cast<const ActChunk*>(act);
+  a.y = y;
+  a.residual = residual;
+  a.rows = rows;
+  a.cols = cols;
+  a.ex = ex;
+  switch (fmt) {
+    case QG_FMT_Q4K_RAW: return launch_exchange_fmt<QG_FMT_Q4K_RAW>(a, stream);
+    case QG_FMT_Q4K_SPLIT_PREDECODED: return launch_exchange_fmt<QG_FMT_Q4K_SPLIT_PREDECODED>(a, stream);
+    case QG_FMT_Q4K_SPLIT_HALF: return launch_exchange_fmt<QG_FMT_Q4K_SPLIT_HALF>(a, stream);
+    case QG_FMT_Q4K_SPLIT_COMPACT: return launch_exchange_fmt<QG_FMT_Q4K_SPLIT_COMPACT>(a, stream);
+    case QG_FMT_Q4K_SPLIT_NATIVE: return launch_exchange_fmt<QG_FMT_Q4K_SPLIT_NATIVE>(a, stream);
+    case QG_FMT_Q5K: return launch_exchange_fmt<QG_FMT_Q5K>(a, stream);
+    case QG_FMT_IQ2S: return launch_exchange_fmt<QG_FMT_IQ2S>(a, stream);
+    case QG_FMT_IQ3S: return launch_exchange_fmt<QG_FMT_IQ3S>(a, stream);
     default: return cudaErrorInvalidValue;
   }
 }

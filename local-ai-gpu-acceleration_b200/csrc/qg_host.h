@@ -30,6 +30,19 @@ cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t sme
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
+// Tensor-parallel exchange of a GEMV's output over NVLink peer memory (qg_decode.cu):
+// every output row is stored into each rank's exchange buffer (this rank's slot, epoch
+// parity half) as one 64-bit word (epoch << 32 | value bits), so a reader knows a word
+// is current from the word itself -- no fence, counter or flag.  The buffers are peer
+// pointers obtained through CUDA IPC.
+constexpr uint32_t kMaxExchangeRanks = 8;
+struct GemvExchange {
+  uint64_t* out[kMaxExchangeRanks];   // per destination rank: this rank's slot, parity 0
+  const uint32_t* epoch;              // exchanges completed on this GPU (the gather advances it)
+  uint32_t n;                         // ranks (0: no exchange)
+  uint32_t stride;                    // words from parity 0 to parity 1
+};
+
 // Launch configuration of the tiled GEMV for one shape (see qg_gemv.cu).
 struct GemvPlan {
   uint32_t grid, threads, group, rpp, passes, rows_per_tile, num_tiles, stages;
@@ -79,6 +92,18 @@ cudaError_t launch_silu_gate(const float* gate, const float* up, uint32_t n, flo
                              cudaStream_t stream);
 
 // h = x * inv_rms(x) * w (+ h's prepared activation); one CTA.
+// y = W x whose rows are also exchanged to every rank (tiled kernel only; returns
+// cudaErrorNotSupported for shapes or alignments that need the fallback kernels).
+cudaError_t launch_gemv_exchange(int fmt, const uint8_t* payload, const uint8_t* meta,
+                                 const float* x, const void* act, float* y, const float* residual,
+                                 uint32_t rows, uint32_t cols, const GemvExchange& ex,
+                                 cudaStream_t stream);
+// Reads every rank's slot, waiting (bounded) for each word of epoch+1, sums the ranks in
+// rank order into x_out, advances the epoch, then RMSNorm*w and h's int8 planes like
+// launch_norm_prepare.
+cudaError_t launch_gather_norm_prepare(const uint64_t* buf, uint32_t* epoch, uint32_t nsrc,
+                                       uint32_t stride, const float* w, uint32_t n, float eps,
+                                       float* x_out, float* h, void* act, cudaStream_t stream);
 cudaError_t launch_norm_prepare(const float* x, const float* w, uint32_t n, float eps, float* h,
                                 void* act, cudaStream_t stream);
 // a = silu(gate) * up (+ a's prepared activation).

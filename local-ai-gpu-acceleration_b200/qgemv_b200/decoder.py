@@ -66,7 +66,7 @@ class DecoderDims(ctypes.Structure):
                                          "ffn", "vocab", "ctx_max")] + [
         ("eps", c_float), ("rope_base", c_float),
         ("attn_fmt", c_int), ("ffn_fmt", c_int), ("down_fmt", c_int), ("head_fmt", c_int),
-        ("tp_rank", c_uint32), ("tp_size", c_uint32)]
+        ("tp_rank", c_uint32), ("tp_size", c_uint32), ("collective", c_uint32)]
 
 
 LAYER_MATS = ("wq", "wk", "wv", "wo", "wg", "wu", "wd")
@@ -79,10 +79,14 @@ class DecoderLayerC(ctypes.Structure):
                 + [("k_cache", c_void_p), ("v_cache", c_void_p)])
 
 
-def dims_struct(spec: ModelSpec, rank: int, tp: int) -> DecoderDims:
+COLLECTIVE_NVLINK = 0  # all-reduces fused into the GEMVs over NVLink peer memory
+COLLECTIVE_NCCL = 1    # ncclAllReduce between the kernels
+
+
+def dims_struct(spec: ModelSpec, rank: int, tp: int, collective: int = COLLECTIVE_NVLINK) -> DecoderDims:
     return DecoderDims(spec.layers, spec.hidden, spec.n_q_heads, spec.n_kv_heads, spec.head_dim,
                        spec.ffn, spec.vocab, spec.ctx_max, spec.eps, spec.rope_base,
-                       spec.attn_fmt, spec.ffn_fmt, spec.down_fmt, spec.head_fmt, rank, tp)
+                       spec.attn_fmt, spec.ffn_fmt, spec.down_fmt, spec.head_fmt, rank, tp, collective)
 
 
 def shard_shape(spec: ModelSpec, rank: int, tp: int) -> dict:
@@ -209,7 +213,7 @@ class Decoder:
     """One rank's decoder: device-resident shards, workspace and the qg_decoder."""
 
     def __init__(self, spec: ModelSpec, weights: dict, rank: int = 0, tp: int = 1,
-                 nccl_id: bytes | None = None, device="cuda"):
+                 nccl_id: bytes | None = None, device="cuda", collective: int = COLLECTIVE_NVLINK):
         self.spec, self.rank, self.tp = spec, rank, tp
         self.device = torch.device(device)
         self._keep = []
@@ -247,7 +251,7 @@ class Decoder:
         fnorm = t(weights["final_norm"]).float().contiguous()
         self._keep.append(fnorm)
         head_p, head_m = pack_ptrs(weights["head"])
-        self.dims = dims_struct(spec, rank, tp)
+        self.dims = dims_struct(spec, rank, tp, collective)
         n = ctypes.c_size_t(0)
         check("qg_decoder_workspace_bytes", ctypes.byref(self.dims), ctypes.byref(n))
         self.workspace = torch.empty(n.value, dtype=torch.uint8, device=dev)

@@ -89,11 +89,15 @@ def test_decoder_graph_replay_matches_eager(cuda):
     dec.close()
 
 
+TP_STEPS = (30, 31, 32)  # positions; the middle step runs as a captured graph
+
+
 def _tp_rank(rank, world, q_in, q_out):
     sys.path.insert(0, str(REPO / "local-ai-gpu-acceleration_b200"))
     import torch
 
     from qgemv_b200 import decoder, packs
+    from qgemv_b200.slice import StepGraph
 
     torch.cuda.set_device(rank)
     spec = decoder.ModelSpec(**SMALL)
@@ -104,24 +108,45 @@ def _tp_rank(rank, world, q_in, q_out):
             q_in.put(nid)
     else:
         nid = q_in.get(timeout=120)
+    dev = f"cuda:{rank}"
     dec = decoder.Decoder(spec, decoder.rank_weights(model, rank, world), rank=rank, tp=world,
-                          nccl_id=nid, device=f"cuda:{rank}")
-    x = torch.from_numpy(packs.synthetic_activation(spec.hidden, 22)).to(f"cuda:{rank}")
-    tok = int(dec.step(x, 30).item())
-    torch.cuda.synchronize()
-    q_out.put((rank, tok, dec.hidden().cpu().numpy()))
+                          nccl_id=nid, device=dev)
+    out = []
+    for i, pos in enumerate(TP_STEPS):
+        x = torch.from_numpy(packs.synthetic_activation(spec.hidden, 22 + i)).to(dev)
+        if i == 1:
+            stream = torch.cuda.Stream(dev)
+            stream.wait_stream(torch.cuda.current_stream(dev))
+            g = StepGraph(stream, lambda: dec.step(x, pos, stream))
+            g.launch()
+            stream.synchronize()
+            g.close()
+            tok = int(dec.token.item())
+        else:
+            tok = int(dec.step(x, pos).item())
+        torch.cuda.synchronize()
+        out.append((tok, dec.hidden().cpu().numpy()))
+    q_out.put((rank, out))
     dec.close()
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
                     reason="needs 2 GPUs")
 def test_decoder_tp2_matches_oracle(port):
+    """Two ranks over NVLink (fused exchange in the Wo / Wd GEMVs, NCCL only for the
+    token all-gather): three consecutive steps -- eager, captured graph, eager -- against
+    the oracle stepping the same model with its caches carried along."""
+    sys.path.insert(0, str(REPO / "oracle"))
+    import decode_oracle
     from qgemv_b200 import decoder, packs
 
     spec = decoder.ModelSpec(**SMALL)
     model = decoder.HostModel.synthetic(spec, seed=21)
-    x = packs.synthetic_activation(spec.hidden, 22)
-    want_tok, want_hidden = _oracle(port, model, x, 30)
+    w = copy.deepcopy(decoder.rank_weights(model, 0, 1))
+    want = []
+    for i, pos in enumerate(TP_STEPS):
+        x = packs.synthetic_activation(spec.hidden, 22 + i)
+        want.append(decode_oracle.step(port, spec, w, x, pos))
     ctx = mp.get_context("spawn")
     q_in, q_out = ctx.Queue(), ctx.Queue()
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
@@ -132,5 +157,9 @@ def test_decoder_tp2_matches_oracle(port):
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
-    for _, tok, hid in res:
-        _check(hid, want_hidden, tok, want_tok)
+    for _, steps in res:
+        for (tok, hid), (want_tok, want_hidden) in zip(steps, want):
+            _check(hid, want_hidden, tok, want_tok)
+    # every rank holds the same bits of the replicated hidden state
+    for (_, a), (_, b) in zip(res[0][1], res[1][1]):
+        assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
