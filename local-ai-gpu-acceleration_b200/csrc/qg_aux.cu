@@ -3,6 +3,8 @@
 // normalisation / gate kernels.
 #include <mutex>
 
+#include <cooperative_groups.h>
+
 #include "qg_formats.cuh"
 #include "qg_host.h"
 
@@ -269,40 +271,52 @@ cudaError_t launch_norm_prepare(const float* x, const float* w, uint32_t n, floa
                   static_cast<ActChunk*>(act));
 }
 
-// Gather of a tensor-parallel exchange + RMSNorm + int8 planes (one CTA).  Every word of
-// every rank's slot carries the epoch it was written for: each is re-read (bounded)
-// until it is current, the ranks are summed in rank order (every rank computes the same
-// bits), x_out is written, the epoch advances, and the vector is normalised exactly like
-// norm_prepare_kernel.
+// Gather of a tensor-parallel exchange + RMSNorm + int8 planes, one thread-block cluster
+// of up to 8 CTAs, CTA c owning elements [c n/C, (c+1) n/C).  Every word of every rank's
+// slot carries the epoch it was written for: a thread issues all ranks' loads of an
+// element at once, re-reads (bounded) any word that is not current yet, and sums the
+// ranks in rank order (every rank computes the same bits).  The sum of squares of the
+// RMSNorm is combined across the cluster through distributed shared memory, in CTA
+// order; no CTA polls global memory for another.
 constexpr uint32_t kMaxWordPolls = 1u << 20;  // per word, with 32 ns sleeps after the first few
 
 __global__ void __launch_bounds__(1024) gather_norm_prepare_kernel(
     const uint64_t* buf, uint32_t* epoch, uint32_t nsrc, uint32_t stride,
     const float* __restrict__ w, uint32_t n, float eps, float* x_out, float* h, ActChunk* act) {
+  namespace cg = cooperative_groups;
+  cg::cluster_group cluster = cg::this_cluster();
   __shared__ float ws[32];
+  __shared__ float part;
   __shared__ uint32_t gave_up;
   pdl_wait();
   pdl_trigger();
+  const uint32_t cta = cluster.block_rank(), ncta = cluster.num_blocks();
   const uint32_t E = *epoch + 1u;
   const uint64_t* base = buf + (E & 1u) * static_cast<size_t>(stride);
   if (threadIdx.x == 0u) gave_up = 0u;
-  __syncthreads();
-  if (threadIdx.x == 0u) *epoch = E;
+  cluster.sync();  // every CTA has read the epoch before it advances
+  if (cta == 0u && threadIdx.x == 0u) *epoch = E;
+  const uint32_t per = n / ncta, lo = cta * per;
   float sq = 0.f;
-  for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
+  for (uint32_t i = lo + threadIdx.x; i < lo + per; i += blockDim.x) {
+    uint64_t word[kMaxExchangeRanks];
+#pragma unroll
+    for (uint32_t s = 0; s < kMaxExchangeRanks; ++s) {
+      if (s < nsrc) word[s] = ld_relaxed_sys_u64(base + static_cast<size_t>(s) * n + i);
+    }
     float v = 0.f;
-    for (uint32_t s = 0; s < nsrc; ++s) {
-      const uint64_t* p = base + static_cast<size_t>(s) * n + i;
-      uint64_t word = ld_relaxed_sys_u64(p);
-      for (uint32_t it = 0; static_cast<uint32_t>(word >> 32) != E; ++it) {
+#pragma unroll
+    for (uint32_t s = 0; s < kMaxExchangeRanks; ++s) {
+      if (s >= nsrc) break;
+      for (uint32_t it = 0; static_cast<uint32_t>(word[s] >> 32) != E; ++it) {
         if (it == kMaxWordPolls || *reinterpret_cast<volatile uint32_t*>(&gave_up) != 0u) {
           if (atomicExch(&gave_up, 1u) == 0u) atomicOr(&g_error_word, QG_ERR_WAIT_TIMEOUT);
           break;
         }
         if (it > 8u) __nanosleep(32);
-        word = ld_relaxed_sys_u64(p);
+        word[s] = ld_relaxed_sys_u64(base + static_cast<size_t>(s) * n + i);
       }
-      v += __uint_as_float(static_cast<uint32_t>(word));
+      v += __uint_as_float(static_cast<uint32_t>(word[s]));
     }
     x_out[i] = v;
     sq += v * v;
@@ -313,12 +327,14 @@ __global__ void __launch_bounds__(1024) gather_norm_prepare_kernel(
   if (threadIdx.x < 32u) {
     sq = threadIdx.x < (blockDim.x >> 5) ? ws[threadIdx.x] : 0.f;
     for (int off = 16; off > 0; off >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, off);
-    if (threadIdx.x == 0u) ws[0] = sq;
+    if (threadIdx.x == 0u) part = sq;
   }
-  __syncthreads();
-  const float inv = 1.0f / sqrtf(ws[0] / static_cast<float>(n) + eps);
+  cluster.sync();  // every CTA's partial sum of squares is in its shared memory
+  float total = 0.f;
+  for (uint32_t c = 0; c < ncta; ++c) total += *cluster.map_shared_rank(&part, c);
+  const float inv = 1.0f / sqrtf(total / static_cast<float>(n) + eps);
   const uint32_t lane = threadIdx.x & 31u;
-  for (uint32_t c = threadIdx.x >> 5; c < n / 64u; c += blockDim.x >> 5) {
+  for (uint32_t c = lo / 64u + (threadIdx.x >> 5); c < (lo + per) / 64u; c += blockDim.x >> 5) {
     const uint32_t i = 64u * c + 2u * lane;
     const float v0 = x_out[i] * inv * w[i], v1 = x_out[i + 1u] * inv * w[i + 1u];
     if (h != nullptr) {
@@ -327,14 +343,32 @@ __global__ void __launch_bounds__(1024) gather_norm_prepare_kernel(
     }
     warp_prepare_chunk(v0, v1, act + c);
   }
+  cluster.sync();  // no CTA leaves while another may still read its partial
 }
 
 cudaError_t launch_gather_norm_prepare(const uint64_t* buf, uint32_t* epoch, uint32_t nsrc,
                                        uint32_t stride, const float* w, uint32_t n, float eps,
                                        float* x_out, float* h, void* act, cudaStream_t stream) {
-  if (nsrc == 0u || nsrc > 32u) return cudaErrorInvalidValue;
-  return launch_k(gather_norm_prepare_kernel, 1, 1024, 0, stream, buf, epoch, nsrc, stride, w, n,
-                  eps, x_out, h, static_cast<ActChunk*>(act));
+  if (nsrc == 0u || nsrc > kMaxExchangeRanks || n % 64u != 0u) return cudaErrorInvalidValue;
+  // CTAs: up to 8, each owning a whole number of 64-column chunks and >= 1024 elements
+  uint32_t ncta = 8u;
+  while (ncta > 1u && (n % (64u * ncta) != 0u || n / ncta < 1024u)) ncta >>= 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(ncta);
+  cfg.blockDim = dim3(1024);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = ncta;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  return cudaLaunchKernelEx(&cfg, gather_norm_prepare_kernel, buf, epoch, nsrc, stride, w, n, eps,
+                            x_out, h, static_cast<ActChunk*>(act));
 }
 
 // a = silu(gate) * up fused with a's activation preparation (one warp per 64 columns;
