@@ -353,7 +353,8 @@ cudaError_t qg_graph_destroy(qg_graph graph);
  * pairs, angle pos * rope_base^(-2i/head_dim)) and cache append at `pos` -> GQA
  * attention over positions [0, pos] -> Wo -> all-reduce (+x) -> rmsnorm -> gate,up ->
  * silu(g)*u -> Wd -> all-reduce (+x1); then final rmsnorm, vocab head and the global
- * argmax (lowest index wins ties) into *token.  head_dim must be 128.  With
+ * argmax (lowest index wins ties) into *token.  head_dim must be 128 and
+ * n_q_heads / n_kv_heads one of 1, 2, 4, 8, 16.  With
  * collective = 0 the all-reduces are fused into the Wo/Wd GEMVs and the following
  * RMSNorm over NVLink peer memory (qg_decoder_create allocates and maps the exchange
  * buffers, up to 8 ranks).  All launches and NCCL collectives go on the caller's stream

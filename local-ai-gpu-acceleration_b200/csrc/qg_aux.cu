@@ -241,38 +241,10 @@ cudaError_t launch_act_prepare(const float* x, uint32_t cols, void* act, cudaStr
                   static_cast<ActChunk*>(act));
 }
 
-// RMSNorm with weights fused with the activation preparation: h = x * inv_rms * w,
-// then h's int8 planes for the GEMVs that read it.  One CTA (the inverse RMS needs
-// the whole vector), one warp per 64-column chunk; h itself is written too when `h`
-// is non-null.
-__global__ void __launch_bounds__(1024) norm_prepare_kernel(const float* __restrict__ x,
-                                                            const float* __restrict__ w,
-                                                            uint32_t n, float eps, float* h,
-                                                            ActChunk* act) {
-  pdl_wait();
-  pdl_trigger();
-  const float sum_sq = block_sum_sq(x, n);
-  const float inv = 1.0f / sqrtf(sum_sq / static_cast<float>(n) + eps);
-  const uint32_t lane = threadIdx.x & 31u;
-  for (uint32_t c = threadIdx.x >> 5; c < n / 64u; c += blockDim.x >> 5) {
-    const uint32_t i = 64u * c + 2u * lane;
-    const float v0 = x[i] * inv * w[i], v1 = x[i + 1u] * inv * w[i + 1u];
-    if (h != nullptr) {
-      h[i] = v0;
-      h[i + 1u] = v1;
-    }
-    warp_prepare_chunk(v0, v1, act + c);
-  }
-}
 
-cudaError_t launch_norm_prepare(const float* x, const float* w, uint32_t n, float eps, float* h,
-                                void* act, cudaStream_t stream) {
-  return launch_k(norm_prepare_kernel, 1, 1024, 0, stream, x, w, n, eps, h,
-                  static_cast<ActChunk*>(act));
-}
-
-// Gather of a tensor-parallel exchange + RMSNorm + int8 planes, one thread-block cluster
-// of up to 8 CTAs, CTA c owning elements [c n/C, (c+1) n/C).  Every word of every rank's
+// RMSNorm + int8 planes of a vector that is either read directly (nsrc = 0: x_in) or
+// gathered from a tensor-parallel exchange, one thread-block cluster of up to 8 CTAs,
+// CTA c owning elements [c n/C, (c+1) n/C).  Every word of every rank's
 // slot carries the epoch it was written for: a thread issues all ranks' loads of an
 // element at once, re-reads (bounded) any word that is not current yet, and sums the
 // ranks in rank order (every rank computes the same bits).  The sum of squares of the
@@ -281,7 +253,7 @@ cudaError_t launch_norm_prepare(const float* x, const float* w, uint32_t n, floa
 constexpr uint32_t kMaxWordPolls = 1u << 20;  // per word, with 32 ns sleeps after the first few
 
 __global__ void __launch_bounds__(1024) gather_norm_prepare_kernel(
-    const uint64_t* buf, uint32_t* epoch, uint32_t nsrc, uint32_t stride,
+    const uint64_t* buf, uint32_t* epoch, uint32_t nsrc, uint32_t stride, const float* x_in,
     const float* __restrict__ w, uint32_t n, float eps, float* x_out, float* h, ActChunk* act) {
   namespace cg = cooperative_groups;
   cg::cluster_group cluster = cg::this_cluster();
@@ -291,11 +263,11 @@ __global__ void __launch_bounds__(1024) gather_norm_prepare_kernel(
   pdl_wait();
   pdl_trigger();
   const uint32_t cta = cluster.block_rank(), ncta = cluster.num_blocks();
-  const uint32_t E = *epoch + 1u;
-  const uint64_t* base = buf + (E & 1u) * static_cast<size_t>(stride);
+  const uint32_t E = nsrc != 0u ? *epoch + 1u : 0u;
+  const uint64_t* base = nsrc != 0u ? buf + (E & 1u) * static_cast<size_t>(stride) : nullptr;
   if (threadIdx.x == 0u) gave_up = 0u;
   cluster.sync();  // every CTA has read the epoch before it advances
-  if (cta == 0u && threadIdx.x == 0u) *epoch = E;
+  if (nsrc != 0u && cta == 0u && threadIdx.x == 0u) *epoch = E;
   const uint32_t per = n / ncta, lo = cta * per;
   float sq = 0.f;
   for (uint32_t i = lo + threadIdx.x; i < lo + per; i += blockDim.x) {
@@ -304,7 +276,7 @@ __global__ void __launch_bounds__(1024) gather_norm_prepare_kernel(
     for (uint32_t s = 0; s < kMaxExchangeRanks; ++s) {
       if (s < nsrc) word[s] = ld_relaxed_sys_u64(base + static_cast<size_t>(s) * n + i);
     }
-    float v = 0.f;
+    float v = nsrc == 0u ? x_in[i] : 0.f;
 #pragma unroll
     for (uint32_t s = 0; s < kMaxExchangeRanks; ++s) {
       if (s >= nsrc) break;
@@ -318,7 +290,7 @@ __global__ void __launch_bounds__(1024) gather_norm_prepare_kernel(
       }
       v += __uint_as_float(static_cast<uint32_t>(word[s]));
     }
-    x_out[i] = v;
+    if (nsrc != 0u) x_out[i] = v;
     sq += v * v;
   }
   for (int off = 16; off > 0; off >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, off);
@@ -334,9 +306,10 @@ __global__ void __launch_bounds__(1024) gather_norm_prepare_kernel(
   for (uint32_t c = 0; c < ncta; ++c) total += *cluster.map_shared_rank(&part, c);
   const float inv = 1.0f / sqrtf(total / static_cast<float>(n) + eps);
   const uint32_t lane = threadIdx.x & 31u;
+  const float* xv = nsrc != 0u ? x_out : x_in;
   for (uint32_t c = lo / 64u + (threadIdx.x >> 5); c < (lo + per) / 64u; c += blockDim.x >> 5) {
     const uint32_t i = 64u * c + 2u * lane;
-    const float v0 = x_out[i] * inv * w[i], v1 = x_out[i + 1u] * inv * w[i + 1u];
+    const float v0 = xv[i] * inv * w[i], v1 = xv[i + 1u] * inv * w[i + 1u];
     if (h != nullptr) {
       h[i] = v0;
       h[i + 1u] = v1;
@@ -346,10 +319,11 @@ __global__ void __launch_bounds__(1024) gather_norm_prepare_kernel(
   cluster.sync();  // no CTA leaves while another may still read its partial
 }
 
-cudaError_t launch_gather_norm_prepare(const uint64_t* buf, uint32_t* epoch, uint32_t nsrc,
-                                       uint32_t stride, const float* w, uint32_t n, float eps,
-                                       float* x_out, float* h, void* act, cudaStream_t stream) {
-  if (nsrc == 0u || nsrc > kMaxExchangeRanks || n % 64u != 0u) return cudaErrorInvalidValue;
+namespace {
+cudaError_t launch_cluster_norm(const uint64_t* buf, uint32_t* epoch, uint32_t nsrc, uint32_t stride,
+                                const float* x_in, const float* w, uint32_t n, float eps,
+                                float* x_out, float* h, void* act, cudaStream_t stream) {
+  if (nsrc > kMaxExchangeRanks || n == 0u || n % 64u != 0u) return cudaErrorInvalidValue;
   // CTAs: up to 8, each owning a whole number of 64-column chunks and >= 1024 elements
   uint32_t ncta = 8u;
   while (ncta > 1u && (n % (64u * ncta) != 0u || n / ncta < 1024u)) ncta >>= 1;
@@ -367,8 +341,23 @@ cudaError_t launch_gather_norm_prepare(const uint64_t* buf, uint32_t* epoch, uin
   attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  return cudaLaunchKernelEx(&cfg, gather_norm_prepare_kernel, buf, epoch, nsrc, stride, w, n, eps,
-                            x_out, h, static_cast<ActChunk*>(act));
+  return cudaLaunchKernelEx(&cfg, gather_norm_prepare_kernel, buf, epoch, nsrc, stride, x_in, w, n,
+                            eps, x_out, h, static_cast<ActChunk*>(act));
+}
+}  // namespace
+
+cudaError_t launch_gather_norm_prepare(const uint64_t* buf, uint32_t* epoch, uint32_t nsrc,
+                                       uint32_t stride, const float* w, uint32_t n, float eps,
+                                       float* x_out, float* h, void* act, cudaStream_t stream) {
+  if (nsrc == 0u || buf == nullptr || epoch == nullptr || x_out == nullptr) return cudaErrorInvalidValue;
+  return launch_cluster_norm(buf, epoch, nsrc, stride, nullptr, w, n, eps, x_out, h, act, stream);
+}
+
+// h = x / sqrt(mean(x^2) + eps) * w and h's int8 planes (the layer slice's and the
+// decoder's RMSNorm; the same cluster kernel reading x directly).
+cudaError_t launch_norm_prepare(const float* x, const float* w, uint32_t n, float eps, float* h,
+                                void* act, cudaStream_t stream) {
+  return launch_cluster_norm(nullptr, nullptr, 0u, 0u, x, w, n, eps, nullptr, h, act, stream);
 }
 
 // a = silu(gate) * up fused with a's activation preparation (one warp per 64 columns;

@@ -72,7 +72,8 @@ bool dims_ok(const qg_decoder_dims* d) {
   if (d == nullptr || d->tp_size == 0u || d->tp_rank >= d->tp_size || d->layers == 0u) return false;
   if (d->head_dim != 128u || d->n_kv_heads == 0u || d->n_q_heads % d->n_kv_heads != 0u) return false;
   if (d->n_q_heads % d->tp_size != 0u || d->n_kv_heads % d->tp_size != 0u) return false;
-  if (d->n_q_heads / d->n_kv_heads > 16u) return false;
+  const uint32_t group = d->n_q_heads / d->n_kv_heads;
+  if (group > 16u || (group & (group - 1u)) != 0u) return false;  // attention: G in {1,2,4,8,16}
   if (d->ffn % d->tp_size != 0u || d->vocab < d->tp_size || d->ctx_max == 0u) return false;
   if (d->collective > 1u || (d->tp_size > 1u && d->collective == 0u && d->tp_size > qg::kMaxExchangeRanks)) {
     return false;
