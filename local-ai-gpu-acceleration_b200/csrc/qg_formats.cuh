@@ -302,18 +302,34 @@ __device__ __forceinline__ void q4_nibble_dot(const uint4 q0, const uint4 q1, co
 // Shared-memory codebook tables of the IQ kernels, replicated so that lookups from
 // one warp spread over the 32 banks instead of colliding (random indices into a
 // single copy cost ~3.5 wavefronts per warp-wide lookup):
-//  * 16 copies of a 4-byte table (IQ3_S grid): word (e*16 + k) for lane k = lane % 16,
-//    so lanes k and k+16 share one bank pair -> at most a 2-way conflict;
+//  * C3 = kIq3Copies copies of a 4-byte table (IQ3_S grid): word (e*C3 + lane % C3);
+//    with 32 copies every lane owns a bank (conflict-free), with 16 lanes k and k+16
+//    share one (at most a 2-way conflict);
 //  * 16 copies of an 8-byte table (sign masks): entry (e*16 + k) sits in bank pair k,
 //    one bank pair per lane of a half-warp -> conflict-free;
-//  * 4 copies of the 8-byte IQ2_S expanded grid: copy r = k % 4 occupies only bank
-//    pairs r, r+4, r+8, r+12, so 4 lanes of a half-warp compete for 4 pairs.
+//  * C = kIq2Copies copies of the 8-byte IQ2_S expanded grid: copy r = k % C occupies
+//    only the bank pairs r + C*i, so 16/C lanes of a half-warp compete for 16/C pairs.
 // The pointers are already offset to this lane's copy, so a lookup is one shifted add:
-// kgrid2[4 e], sign2[16 e], grid3[16 e], sign3[16 e].
+// kgrid2[C e], sign2[16 e], grid3[C3 e], sign3[16 e].
+#ifndef QG_IQ2S_KGRID_COPIES
+#define QG_IQ2S_KGRID_COPIES 8u
+#endif
+constexpr uint32_t kIq2Copies = QG_IQ2S_KGRID_COPIES;
+static_assert(kIq2Copies == 4u || kIq2Copies == 8u, "IQ2_S grid copies: 4 or 8");
+constexpr uint32_t kIq2SignWord = 2048u * kIq2Copies;  // word offset of the IQ2_S sign table
+constexpr uint32_t kIq2TableBytes = (kIq2SignWord + 8192u) * 4u;
+#ifndef QG_IQ3S_GRID_COPIES
+#define QG_IQ3S_GRID_COPIES 32u
+#endif
+constexpr uint32_t kIq3Copies = QG_IQ3S_GRID_COPIES;
+static_assert(kIq3Copies == 16u || kIq3Copies == 32u, "IQ3_S grid copies: 16 or 32");
+constexpr uint32_t kIq3SignByte = 2048u * kIq3Copies;  // byte offset of the IQ3_S sign table
+constexpr uint32_t kIq3TableBytes = kIq3SignByte + 32768u;
+
 struct IqTables {
-  const uint2* kgrid2;    // IQ2_S: 1024 entries x 4 copies (slot 4e + k%4), 8 bytes 2k
+  const uint2* kgrid2;    // IQ2_S: 1024 entries x C copies (slot C e + k%C), 8 bytes 2k
   const uint2* sign2;     // IQ2_S: 256 entries x 16 copies (slot 16e + k), bytes (sign ? 0x0E : 0)
-  const uint32_t* grid3;  // IQ3_S: 512 entries x 16 copies (slot 16e + k), 4 magnitudes
+  const uint32_t* grid3;  // IQ3_S: 512 entries x C3 copies (slot C3 e + lane%C3), 4 magnitudes
   const uint2* sign3;     // IQ3_S: 256 entries x 16 copies (slot 16e + k), bytes (sign ? 0x1E : 0)
   uint32_t k;             // lane % 16
 };
@@ -454,7 +470,7 @@ __device__ __forceinline__ float chunk_dot<QG_FMT_IQ2S>(const uint8_t* rp, const
 #pragma unroll
     for (int g = 0; g < 4; ++g) {
       const uint32_t idx = byte_of(gl[ib], g) | ((qhb << (8 - 2 * g)) & 0x300u);
-      const uint2 k2 = t.kgrid2[idx << 2];
+      const uint2 k2 = t.kgrid2[idx * kIq2Copies];
       const uint2 sm = t.sign2[byte_of(sg[ib], g) << 4];
       const uint32_t u0 = k2.x ^ sm.x ^ 0x09090909u;
       const uint32_t u1 = k2.y ^ sm.y ^ 0x09090909u;
@@ -500,7 +516,7 @@ __device__ __forceinline__ float chunk_dot<QG_FMT_IQ3S>(const uint8_t* rp, const
         const int sel = 2 * g + p;
         const uint32_t qb = byte_of(qs[2 * ib + (sel >> 2)], sel & 3);
         const uint32_t idx = qb | (((qhb >> sel) & 1u) << 8u);
-        const uint32_t u = t.grid3[idx << 4] ^ 0x11111111u ^ (p ? sm.y : sm.x);
+        const uint32_t u = t.grid3[idx * kIq3Copies] ^ 0x11111111u ^ (p ? sm.y : sm.x);
         ih = dp4a(u, H[sel], ih);
         il = dp4a(u, Lp[sel], il);
       }
@@ -514,11 +530,11 @@ __device__ __forceinline__ float chunk_dot<QG_FMT_IQ3S>(const uint8_t* rp, const
   return res;
 }
 
-// The replicated tables, built at compile time from the codebooks (64 KB per IQ
-// format, in the IqTables layout) and copied into each CTA's shared memory with one
-// bulk copy.
+// The replicated tables, built at compile time from the codebooks (in the IqTables
+// layout: kIq2TableBytes for IQ2_S, 64 KB for IQ3_S) and copied into each CTA's
+// shared memory with one bulk copy.
 struct __align__(16) ReplicatedTables {
-  uint32_t w[16384];
+  uint32_t w[(kIq2TableBytes > kIq3TableBytes ? kIq2TableBytes : kIq3TableBytes) / 4u];
 };
 
 namespace tables_detail {
@@ -548,22 +564,22 @@ constexpr ReplicatedTables make_iq2s() {
       lo |= (((G >> (2u * l)) & 3u) << 1) << (8u * l);
       hi |= (((G >> (2u * (l + 4u))) & 3u) << 1) << (8u * l);
     }
-    for (uint32_t r = 0; r < 4u; ++r) {
-      const uint32_t slot = 4u * e + r;
+    for (uint32_t r = 0; r < kIq2Copies; ++r) {
+      const uint32_t slot = kIq2Copies * e + r;
       t.w[2u * slot] = lo;
       t.w[2u * slot + 1u] = hi;
     }
   }
-  put_sign_copies(t, 8192u, 0x0eu);
+  put_sign_copies(t, kIq2SignWord, 0x0eu);
   return t;
 }
 
 constexpr ReplicatedTables make_iq3s() {
   ReplicatedTables t{};
   for (uint32_t e = 0; e < 512u; ++e) {
-    for (uint32_t r = 0; r < 16u; ++r) t.w[(e << 4) | r] = kIq3Grid[e];
+    for (uint32_t r = 0; r < kIq3Copies; ++r) t.w[e * kIq3Copies + r] = kIq3Grid[e];
   }
-  put_sign_copies(t, 8192u, 0x1eu);
+  put_sign_copies(t, kIq3SignByte / 4u, 0x1eu);
   return t;
 }
 }  // namespace tables_detail
@@ -582,7 +598,8 @@ __device__ __forceinline__ void build_iq_tables(uint8_t* base, uint32_t tid, uin
   if (FMT == QG_FMT_IQ2S || FMT == QG_FMT_IQ3S) {
     const uint4* src = reinterpret_cast<const uint4*>(replicated_tables<FMT>());
     uint4* dst = reinterpret_cast<uint4*>(base);
-    for (uint32_t i = tid; i < 4096u; i += n) dst[i] = __ldg(src + i);
+    constexpr uint32_t kVecs = (FMT == QG_FMT_IQ2S ? kIq2TableBytes : kIq3TableBytes) / 16u;
+    for (uint32_t i = tid; i < kVecs; i += n) dst[i] = __ldg(src + i);
   }
 }
 
@@ -591,17 +608,17 @@ __device__ __forceinline__ IqTables iq_tables(const uint8_t* base, uint32_t lane
   IqTables t{};
   t.k = lane & 15u;
   if (FMT == QG_FMT_IQ2S) {
-    t.kgrid2 = reinterpret_cast<const uint2*>(base) + (t.k & 3u);
-    t.sign2 = reinterpret_cast<const uint2*>(base) + 4096 + t.k;
+    t.kgrid2 = reinterpret_cast<const uint2*>(base) + (t.k & (kIq2Copies - 1u));
+    t.sign2 = reinterpret_cast<const uint2*>(base) + kIq2SignWord / 2u + t.k;
   } else if (FMT == QG_FMT_IQ3S) {
-    t.grid3 = reinterpret_cast<const uint32_t*>(base) + t.k;
-    t.sign3 = reinterpret_cast<const uint2*>(base + 32768) + t.k;
+    t.grid3 = reinterpret_cast<const uint32_t*>(base) + (lane & (kIq3Copies - 1u));
+    t.sign3 = reinterpret_cast<const uint2*>(base + kIq3SignByte) + t.k;
   }
   return t;
 }
 
 constexpr uint32_t iq_table_bytes(int fmt) {
-  return fmt == QG_FMT_IQ2S ? 65536u : fmt == QG_FMT_IQ3S ? 65536u : 0u;
+  return fmt == QG_FMT_IQ2S ? kIq2TableBytes : fmt == QG_FMT_IQ3S ? kIq3TableBytes : 0u;
 }
 
 // A prepared activation: x quantized once (qg_act_prepare) into one 176-byte record

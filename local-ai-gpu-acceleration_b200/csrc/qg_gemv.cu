@@ -11,8 +11,13 @@
 //  * Consumer thread (slot, c) owns the 64-column chunk c: its x values are loaded
 //    once, as two int8 planes, and every row's chunk is a string of dp4a
 //    instructions (qg_formats.cuh).  Row sums: shuffle reduction in lane groups of
-//    gcd(cols/64, 32), shared-memory partials, one consumer barrier per tile, then
-//    the epilogue (y, optional residual, the reference's KV page word).
+//    gcd(cols/64, 32) (for full-warp groups and stages of 4k passes, four rows at a
+//    time with one transposed butterfly), shared-memory partials, one consumer
+//    barrier per tile, then the epilogue (y, optional residual, the reference's KV
+//    page word).
+//  * IQ formats (issue- and shared-memory-bound, not HBM-bound): 16 consumer warps,
+//    one CTA per SM, stages of four passes, codebooks replicated in shared memory
+//    so that table lookups spread over the banks (qg_formats.cuh).
 //  * Every mbarrier wait is bounded (QG_ERR_WAIT_TIMEOUT); the producer waits for its
 //    copies in flight before it exits.
 // gemv_staged_kernel<FMT> handles packs whose base address is not 16-B aligned
@@ -82,6 +87,7 @@ struct GemvArgs {
   const ActChunk* xq;     // prepared activation (qg_act_prepare), or null: quantize x here
   GemvSeg seg[kMaxSegs];  // tiled kernel: the matrices of this launch (seg[0] = payload/meta/y)
   uint32_t nseg;
+  uint32_t red4;          // tiled kernel: passes reduced four at a time (group 32, Q % 4 == 0)
   GemvExchange ex;        // tiled kernel: optional tensor-parallel exchange of the rows
 };
 
@@ -321,6 +327,21 @@ __device__ __forceinline__ float group_sum(float v, uint32_t group) {
   return v;
 }
 
+// Sums four per-lane values over the 32 lanes of a warp at once, a transposed
+// butterfly: the first two exchanges trade one value of a pair instead of both
+// (6 shuffles for four sums instead of 20).  Lane l ends with the total of
+// v[2 * bit3(l) + bit4(l)], so lanes 0, 16, 8, 24 hold the sums of v[0..3].
+__device__ __forceinline__ float warp_sum4(const float (&v)[4], uint32_t lane) {
+  const bool b4 = (lane & 16u) != 0u, b3 = (lane & 8u) != 0u;
+  const float w0 = (b4 ? v[1] : v[0]) + __shfl_xor_sync(0xffffffffu, b4 ? v[0] : v[1], 16);
+  const float w1 = (b4 ? v[3] : v[2]) + __shfl_xor_sync(0xffffffffu, b4 ? v[2] : v[3], 16);
+  float u = (b3 ? w1 : w0) + __shfl_xor_sync(0xffffffffu, b3 ? w0 : w1, 8);
+  u += __shfl_xor_sync(0xffffffffu, u, 4);
+  u += __shfl_xor_sync(0xffffffffu, u, 2);
+  u += __shfl_xor_sync(0xffffffffu, u, 1);
+  return u;
+}
+
 template <int FMT>
 __global__ void __launch_bounds__(544, 1) gemv_tiled_kernel(const GemvArgs a) {
   constexpr uint32_t PB = FmtTraits<FMT>::payload_bytes;
@@ -356,8 +377,8 @@ __global__ void __launch_bounds__(544, 1) gemv_tiled_kernel(const GemvArgs a) {
       const uint64_t policy = l2_evict_first_policy();
       if (kTables) {
         // The codebook tables (64 KB, L2-resident after the first CTA) in one bulk copy.
-        mbar_arrive_expect_tx(table_bar, sizeof(ReplicatedTables));
-        tma_load_1d(smem + a.table_off, replicated_tables<FMT>(), sizeof(ReplicatedTables),
+        mbar_arrive_expect_tx(table_bar, iq_table_bytes(FMT));
+        tma_load_1d(smem + a.table_off, replicated_tables<FMT>(), iq_table_bytes(FMT),
                     table_bar);
       }
       bool ok = true;
@@ -428,8 +449,28 @@ __global__ void __launch_bounds__(544, 1) gemv_tiled_kernel(const GemvArgs a) {
       if (!mbar_wait_bounded(&full[s], phase)) failed = true;
       const uint8_t* st = stages + s * a.stage_bytes;
       const uint32_t lr0 = j * a.stage_rows + slot;  // tile row of q = 0
+      if (a.red4 != 0u) {
+        // A warp covers 32 chunks of one row slot: four passes' chunks, then one
+        // transposed reduction for the four rows.
+        for (uint32_t q = 0; q < Q; q += 4u) {
+          float v[4];
+#pragma unroll
+          for (uint32_t r = 0; r < 4u; ++r) {
+            const uint32_t lr = lr0 + (q + r) * a.rpp;
+            v[r] = 0.f;
+            if (valid && lr < nrows && !failed) {
+              const uint32_t ls = (q + r) * a.rpp + slot;
+              v[r] = chunk_dot<FMT>(st + ls * row_stride, st + a.meta_off + ls * meta_stride, c,
+                                    xr, tables);
+            }
+          }
+          const float u = warp_sum4(v, lane);
+          const uint32_t lr = lr0 + (q + (((lane >> 2) & 2u) | ((lane >> 4) & 1u))) * a.rpp;
+          if ((lane & 7u) == 0u && valid && lr < nrows && !failed) rb[lr * gpr + gidx] = u;
+        }
+      }
 #pragma unroll 2
-      for (uint32_t q = 0; q < Q; ++q) {
+      for (uint32_t q = 0; a.red4 == 0u && q < Q; ++q) {
         const uint32_t lr = lr0 + q * a.rpp;
         const bool live = valid && lr < nrows && !failed;
         float part = 0.f;
@@ -451,7 +492,7 @@ __global__ void __launch_bounds__(544, 1) gemv_tiled_kernel(const GemvArgs a) {
     consumer_sync(nconsumers);
     for (uint32_t t = tid; t < nrows; t += nconsumers) {
       float v = 0.f;
-      for (uint32_t g = 0; g < gpr; ++g) v += rb[t * gpr + g];
+      for (uint32_t k = 0; k < gpr; ++k) v += rb[t * gpr + k];
       const uint32_t row = row0 + t;
       if (a.residual != nullptr) v += a.residual[row];
       g.y[row] = v;
@@ -555,6 +596,7 @@ void fill_args(GemvArgs& a, const GemvPlan& plan) {
   a.stage_rows = plan.stage_rows;
   a.stage_mask = plan.stage_passes - 1u;
   a.stage_shift = static_cast<uint32_t>(__builtin_ctz(plan.stage_passes));
+  a.red4 = (plan.tiled != 0u && plan.group == 32u && (plan.stage_passes & 3u) == 0u) ? 1u : 0u;
 }
 
 template <int FMT>
@@ -649,12 +691,25 @@ cudaError_t launch_multi_fmt(GemvArgs a, uint32_t nseg, const GemvSeg* segs, cud
 
 // Threads per CTA: rows-per-pass is the smallest multiple of 32/group (whole warps)
 // that reaches ~256 threads; rows wider than 512 threads pad the last warp.
-void plan_threads(uint32_t tpr, GemvPlan& p) {
+#ifndef QG_IQ_THREADS
+#define QG_IQ_THREADS 512u
+#endif
+#ifndef QG_IQ_STAGE_PASSES
+#define QG_IQ_STAGE_PASSES 4u
+#endif
+#ifndef QG_IQ_STAGE_BUDGET
+#define QG_IQ_STAGE_BUDGET (96u * 1024u)
+#endif
+constexpr uint32_t kIqThreads = QG_IQ_THREADS;
+constexpr uint32_t kIqStagePasses = QG_IQ_STAGE_PASSES;
+constexpr uint32_t kIqStageBudget = QG_IQ_STAGE_BUDGET;
+
+void plan_threads(uint32_t tpr, GemvPlan& p, uint32_t limit = 256u) {
   p.group = gcd_u32(tpr, 32u);
   const uint32_t base = 32u / p.group;
   uint32_t rpp = base;
   if (rpp * tpr > 512u) rpp = 1u;
-  while ((rpp + base) * tpr <= 256u) rpp += base;
+  while ((rpp + base) * tpr <= limit) rpp += base;
   p.rpp = rpp;
   p.threads = ((rpp * tpr + 31u) / 32u) * 32u;
 }
@@ -679,13 +734,15 @@ uint32_t ctas_per_sm(const GemvPlan& p) {
 
 // Plan of the tiled kernel.  passes P in {32, 16, 8, 4}: the largest that still gives
 // every resident CTA at least two tiles; stage = Q passes (Q | P) of ~16 KB whose
-// byte count is a multiple of 16; S stages within ~96 KB (2..8).
+// byte count is a multiple of 16 (IQ formats: at least four passes); S stages within
+// ~96 KB (2..8).
 GemvPlan plan_gemv(int fmt, uint32_t rows, uint32_t cols, int sms) {
   GemvPlan p{};
   const uint32_t PB = qg_payload_bytes_per_block(fmt);
   const uint32_t MB = qg_meta_bytes_per_block(fmt);
   const uint32_t bpr = cols >> 8, tpr = cols / 64u;
-  plan_threads(tpr, p);
+  const bool iq = iq_table_bytes(fmt) != 0u;
+  plan_threads(tpr, p, iq ? kIqThreads : 256u);
   const uint32_t row_bytes = bpr * PB, row_meta = bpr * MB;
   // Stage: smallest power-of-two passes with 16-B aligned bytes, grown toward 16 KB.
   uint32_t q = 1u;
@@ -697,8 +754,11 @@ GemvPlan plan_gemv(int fmt, uint32_t rows, uint32_t cols, int sms) {
     return p;
   }
   const uint32_t q_align = q;
-  const uint32_t stage_target = iq_table_bytes(fmt) ? 8192u : 16384u;
+  const uint32_t stage_target = iq ? 8192u : 16384u;
   while (q < 16u && 2u * q * p.rpp * (row_bytes + row_meta) <= stage_target) q <<= 1;
+  // IQ readers are issue-bound: four passes per stage give every thread four
+  // independent chunks and one transposed reduction per four rows.
+  if (iq && p.group == 32u) q = std::max(q, kIqStagePasses);
   const uint32_t resident = static_cast<uint32_t>(sms) * 2u;
   uint32_t P = 32u;
   while (P > 4u && (rows + P * p.rpp - 1u) / (P * p.rpp) < 2u * resident) P >>= 1;
@@ -712,7 +772,7 @@ GemvPlan plan_gemv(int fmt, uint32_t rows, uint32_t cols, int sms) {
   const uint32_t pay = p.stage_rows * row_bytes, met = p.stage_rows * row_meta;
   p.meta_off = (pay + 127u) & ~127u;
   p.stage_bytes = MB ? ((p.meta_off + met + 127u) & ~127u) : ((pay + 127u) & ~127u);
-  const uint32_t budget = iq_table_bytes(fmt) ? 40u * 1024u : 96u * 1024u;
+  const uint32_t budget = iq ? kIqStageBudget : 96u * 1024u;
   p.stages = std::max(2u, std::min(8u, budget / p.stage_bytes));
   p.threads += 32u;  // producer warp
   plan_smem(fmt, tpr, p);
