@@ -723,21 +723,50 @@ void plan_smem(int fmt, uint32_t tpr, GemvPlan& p) {
   p.smem_bytes = p.stage_off + p.stages * p.stage_bytes;
 }
 
+// Resident CTAs per SM of a plan (the tiled kernels are built for <= 96 registers).
 uint32_t ctas_per_sm(const GemvPlan& p) {
   const uint32_t by_smem = std::max(1u, (228u * 1024u) / (p.smem_bytes + 1024u));
   const uint32_t by_threads = std::max(1u, 2048u / p.threads);
-  const uint32_t by_regs = std::max(1u, 65536u / (p.threads * 128u));
+  const uint32_t by_regs = std::max(1u, 65536u / (((p.threads + 31u) / 32u) * 32u * 96u));
   return std::min(by_smem, std::min(by_threads, by_regs));
+}
+
+// Passes per tile.  Tiles go round-robin to the G = min(T, slots) persistent CTAs, so
+// CTA j runs ceil(T / G) or one fewer tiles, and an SM runs whichever m CTAs the block
+// scheduler put on it (m = CTAs per SM when G exceeds the SM count, else 1).  Cost of
+// a tile size P (a multiple of the stage's q passes, at most 128): the tiles of the m
+// busiest CTAs times (P + 1/2) -- the half pass stands for a tile's barrier and
+// epilogue -- divided by 0.6 when a CTA sized to share its SM runs alone (measured on
+// B200: one 9-warp CTA streams ~0.6 of what two do).  Ties go to the larger P.
+uint32_t balanced_passes(uint32_t total_passes, uint32_t q, uint32_t sms, uint32_t cps) {
+  const uint32_t slots = sms * cps;
+  uint32_t best_p = q;
+  double best_cost = 1e300;
+  for (uint32_t P = q; P <= std::max(q, 128u); P += q) {
+    const uint32_t T = (total_passes + P - 1u) / P;
+    const uint32_t G = std::min(T, slots);
+    const uint32_t k = (T + G - 1u) / G;         // tiles of the busiest CTAs
+    const uint32_t n_k = T - (k - 1u) * G;        // CTAs with k tiles
+    const uint32_t m = G > sms ? cps : 1u;        // CTAs sharing the busiest SM
+    const uint32_t tiles = n_k >= m ? m * k : n_k * k + (m - n_k) * (k - 1u);
+    double cost = static_cast<double>(tiles) * (2.0 * P + 1.0);
+    if (cps > 1u && G <= sms) cost /= 0.6;
+    if (cost <= best_cost) {
+      best_cost = cost;
+      best_p = P;
+    }
+  }
+  return best_p;
 }
 
 }  // namespace
 
-// Plan of the tiled kernel.  passes P in {32, 16, 8, 4}: the largest that still gives
-// every resident CTA at least two tiles; stage = Q passes (Q | P) of ~16 KB whose
-// byte count is a multiple of 16 (IQ formats: at least four passes); S stages within
-// ~96 KB (2..8).
+// Plan of the tiled kernel.  Stage = Q passes of ~16 KB whose byte count is a multiple
+// of 16 (IQ formats: at least four passes); S stages within ~96 KB (2..8); tiles of P
+// passes (Q | P) balanced over the SMs (balanced_passes).
 GemvPlan plan_gemv(int fmt, uint32_t rows, uint32_t cols, int sms) {
   GemvPlan p{};
+  sms = std::max(sms, 1);  // no device (host-side plan query): plan for one SM
   const uint32_t PB = qg_payload_bytes_per_block(fmt);
   const uint32_t MB = qg_meta_bytes_per_block(fmt);
   const uint32_t bpr = cols >> 8, tpr = cols / 64u;
@@ -759,22 +788,27 @@ GemvPlan plan_gemv(int fmt, uint32_t rows, uint32_t cols, int sms) {
   // IQ readers are issue-bound: four passes per stage give every thread four
   // independent chunks and one transposed reduction per four rows.
   if (iq && p.group == 32u) q = std::max(q, kIqStagePasses);
-  const uint32_t resident = static_cast<uint32_t>(sms) * 2u;
-  uint32_t P = 32u;
-  while (P > 4u && (rows + P * p.rpp - 1u) / (P * p.rpp) < 2u * resident) P >>= 1;
-  P = std::max(P, q_align);  // a stage is never smaller than its aligned size
-  q = std::min(q, P);        // both powers of two >= q_align: q stays aligned
-  p.passes = P;
+  const uint32_t total_passes = std::max(1u, (rows + p.rpp - 1u) / p.rpp);
+  // Small matrices: a stage is never more passes than the matrix has (but never less
+  // than its 16-B aligned size).
+  while (q > q_align && q > total_passes) q >>= 1;
   p.stage_passes = q;
   p.stage_rows = q * p.rpp;
-  p.rows_per_tile = P * p.rpp;
-  p.num_tiles = (rows + p.rows_per_tile - 1u) / p.rows_per_tile;
   const uint32_t pay = p.stage_rows * row_bytes, met = p.stage_rows * row_meta;
   p.meta_off = (pay + 127u) & ~127u;
   p.stage_bytes = MB ? ((p.meta_off + met + 127u) & ~127u) : ((pay + 127u) & ~127u);
   const uint32_t budget = iq ? kIqStageBudget : 96u * 1024u;
   p.stages = std::max(2u, std::min(8u, budget / p.stage_bytes));
   p.threads += 32u;  // producer warp
+  // Resident CTAs per SM from the smallest tile, then the balanced tile size.
+  p.passes = q;
+  p.rows_per_tile = q * p.rpp;
+  plan_smem(fmt, tpr, p);
+  const uint32_t cps = ctas_per_sm(p);
+  const uint32_t P = balanced_passes(total_passes, q, static_cast<uint32_t>(sms), cps);
+  p.passes = P;
+  p.rows_per_tile = P * p.rpp;
+  p.num_tiles = (rows + p.rows_per_tile - 1u) / p.rows_per_tile;
   plan_smem(fmt, tpr, p);
   p.grid = std::max(1u, std::min(p.num_tiles, static_cast<uint32_t>(sms) * ctas_per_sm(p)));
   p.tiled = 1u;
