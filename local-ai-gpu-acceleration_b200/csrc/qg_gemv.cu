@@ -87,7 +87,7 @@ struct GemvArgs {
   const ActChunk* xq;     // prepared activation (qg_act_prepare), or null: quantize x here
   GemvSeg seg[kMaxSegs];  // tiled kernel: the matrices of this launch (seg[0] = payload/meta/y)
   uint32_t nseg;
-  uint32_t red4;          // tiled kernel: passes reduced four at a time (group 32, Q % 4 == 0)
+  uint32_t red;           // tiled kernel: passes reduced 4 or 2 at a time (group 32, Q % red == 0), else 0
   GemvExchange ex;        // tiled kernel: optional tensor-parallel exchange of the rows
 };
 
@@ -342,6 +342,18 @@ __device__ __forceinline__ float warp_sum4(const float (&v)[4], uint32_t lane) {
   return u;
 }
 
+// The two-value form: lane l ends with the total of v[bit4(l)] (lanes 0 and 16 hold
+// the sums of v[0] and v[1]); 5 shuffles instead of 10.
+__device__ __forceinline__ float warp_sum2(const float (&v)[2], uint32_t lane) {
+  const bool b4 = (lane & 16u) != 0u;
+  float u = (b4 ? v[1] : v[0]) + __shfl_xor_sync(0xffffffffu, b4 ? v[0] : v[1], 16);
+  u += __shfl_xor_sync(0xffffffffu, u, 8);
+  u += __shfl_xor_sync(0xffffffffu, u, 4);
+  u += __shfl_xor_sync(0xffffffffu, u, 2);
+  u += __shfl_xor_sync(0xffffffffu, u, 1);
+  return u;
+}
+
 template <int FMT>
 __global__ void __launch_bounds__(544, 1) gemv_tiled_kernel(const GemvArgs a) {
   constexpr uint32_t PB = FmtTraits<FMT>::payload_bytes;
@@ -449,7 +461,7 @@ __global__ void __launch_bounds__(544, 1) gemv_tiled_kernel(const GemvArgs a) {
       if (!mbar_wait_bounded(&full[s], phase)) failed = true;
       const uint8_t* st = stages + s * a.stage_bytes;
       const uint32_t lr0 = j * a.stage_rows + slot;  // tile row of q = 0
-      if (a.red4 != 0u) {
+      if (a.red == 4u) {
         // A warp covers 32 chunks of one row slot: four passes' chunks, then one
         // transposed reduction for the four rows.
         for (uint32_t q = 0; q < Q; q += 4u) {
@@ -468,9 +480,26 @@ __global__ void __launch_bounds__(544, 1) gemv_tiled_kernel(const GemvArgs a) {
           const uint32_t lr = lr0 + (q + (((lane >> 2) & 2u) | ((lane >> 4) & 1u))) * a.rpp;
           if ((lane & 7u) == 0u && valid && lr < nrows && !failed) rb[lr * gpr + gidx] = u;
         }
+      } else if (a.red == 2u) {
+        for (uint32_t q = 0; q < Q; q += 2u) {
+          float v[2];
+#pragma unroll
+          for (uint32_t r = 0; r < 2u; ++r) {
+            const uint32_t lr = lr0 + (q + r) * a.rpp;
+            v[r] = 0.f;
+            if (valid && lr < nrows && !failed) {
+              const uint32_t ls = (q + r) * a.rpp + slot;
+              v[r] = chunk_dot<FMT>(st + ls * row_stride, st + a.meta_off + ls * meta_stride, c,
+                                    xr, tables);
+            }
+          }
+          const float u = warp_sum2(v, lane);
+          const uint32_t lr = lr0 + (q + (lane >> 4)) * a.rpp;
+          if ((lane & 15u) == 0u && valid && lr < nrows && !failed) rb[lr * gpr + gidx] = u;
+        }
       }
 #pragma unroll 2
-      for (uint32_t q = 0; a.red4 == 0u && q < Q; ++q) {
+      for (uint32_t q = 0; a.red == 0u && q < Q; ++q) {
         const uint32_t lr = lr0 + q * a.rpp;
         const bool live = valid && lr < nrows && !failed;
         float part = 0.f;
@@ -596,7 +625,10 @@ void fill_args(GemvArgs& a, const GemvPlan& plan) {
   a.stage_rows = plan.stage_rows;
   a.stage_mask = plan.stage_passes - 1u;
   a.stage_shift = static_cast<uint32_t>(__builtin_ctz(plan.stage_passes));
-  a.red4 = (plan.tiled != 0u && plan.group == 32u && (plan.stage_passes & 3u) == 0u) ? 1u : 0u;
+  a.red = 0u;
+  if (plan.tiled != 0u && plan.group == 32u) {
+    a.red = (plan.stage_passes & 3u) == 0u ? 4u : (plan.stage_passes & 1u) == 0u ? 2u : 0u;
+  }
 }
 
 template <int FMT>
@@ -697,11 +729,21 @@ cudaError_t launch_multi_fmt(GemvArgs a, uint32_t nseg, const GemvSeg* segs, cud
 #ifndef QG_IQ_STAGE_PASSES
 #define QG_IQ_STAGE_PASSES 4u
 #endif
+#ifndef QG_STAGE_PASSES
+#define QG_STAGE_PASSES 4u
+#endif
+#ifndef QG_THREADS
+#define QG_THREADS 256u
+#endif
 #ifndef QG_IQ_STAGE_BUDGET
 #define QG_IQ_STAGE_BUDGET (96u * 1024u)
 #endif
 constexpr uint32_t kIqThreads = QG_IQ_THREADS;
 constexpr uint32_t kIqStagePasses = QG_IQ_STAGE_PASSES;
+constexpr uint32_t kStagePasses = QG_STAGE_PASSES;
+constexpr uint32_t kThreads = QG_THREADS;
+// Dynamic shared memory a CTA may opt into on sm_100 (227 KB).
+constexpr uint32_t kSmemOptinMax = 232448u;
 constexpr uint32_t kIqStageBudget = QG_IQ_STAGE_BUDGET;
 
 void plan_threads(uint32_t tpr, GemvPlan& p, uint32_t limit = 256u) {
@@ -771,7 +813,7 @@ GemvPlan plan_gemv(int fmt, uint32_t rows, uint32_t cols, int sms) {
   const uint32_t MB = qg_meta_bytes_per_block(fmt);
   const uint32_t bpr = cols >> 8, tpr = cols / 64u;
   const bool iq = iq_table_bytes(fmt) != 0u;
-  plan_threads(tpr, p, iq ? kIqThreads : 256u);
+  plan_threads(tpr, p, iq ? kIqThreads : kThreads);
   const uint32_t row_bytes = bpr * PB, row_meta = bpr * MB;
   // Stage: smallest power-of-two passes with 16-B aligned bytes, grown toward 16 KB.
   uint32_t q = 1u;
@@ -787,11 +829,20 @@ GemvPlan plan_gemv(int fmt, uint32_t rows, uint32_t cols, int sms) {
   while (q < 16u && 2u * q * p.rpp * (row_bytes + row_meta) <= stage_target) q <<= 1;
   // IQ readers are issue-bound: four passes per stage give every thread four
   // independent chunks and one transposed reduction per four rows.
-  if (iq && p.group == 32u) q = std::max(q, kIqStagePasses);
+  if (p.group == 32u) q = std::max(q, iq ? kIqStagePasses : kStagePasses);
   const uint32_t total_passes = std::max(1u, (rows + p.rpp - 1u) / p.rpp);
   // Small matrices: a stage is never more passes than the matrix has (but never less
   // than its 16-B aligned size).
   while (q > q_align && q > total_passes) q >>= 1;
+  // Two stages of q passes, the codebooks and a worst-case reduction buffer must fit the
+  // 227 KB a CTA may opt into (else the launch would drop to the all-thread kernels).
+  auto fits = [&](uint32_t qq) {
+    const uint32_t stage = ((qq * p.rpp * row_bytes + 127u) & ~127u) +
+                           ((qq * p.rpp * row_meta + 127u) & ~127u);
+    const uint32_t red = 2u * 128u * p.rpp * (tpr / p.group) * 4u;
+    return 2u * stage + red + iq_table_bytes(fmt) + 1024u <= kSmemOptinMax;
+  };
+  while (q > q_align && !fits(q)) q >>= 1;
   p.stage_passes = q;
   p.stage_rows = q * p.rpp;
   const uint32_t pay = p.stage_rows * row_bytes, met = p.stage_rows * row_meta;
