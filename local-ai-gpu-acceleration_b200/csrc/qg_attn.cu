@@ -5,10 +5,11 @@
 //  * rope_append_kernel: rotary position embedding of this rank's q and k heads
 //    (adjacent pairs (2i, 2i+1), angle pos * base^(-2i/head_dim)), then k and v of the
 //    new position written to the fp16 KV cache.
-//  * attn_split_kernel + attn_combine_kernel: grouped-query decode attention over the
-//    fp16 cache (flash-decoding: one CTA per (kv head, span of positions) computes the
-//    span's max, sum and weighted V for all q heads of the group; the combine merges
-//    the spans, normalises and emits the Wo GEMV's int8 planes).
+//  * attn_split_tc_kernel (groups <= 8, tensor cores) or attn_split_kernel (CUDA cores)
+//    + attn_combine_kernel: grouped-query decode attention over the fp16 cache
+//    (flash-decoding: one CTA per (kv head, span of positions) computes the span's max,
+//    sum and weighted V for all q heads of the group; the combine merges the spans,
+//    normalises and emits the Wo GEMV's int8 planes).
 //  * argmax_candidate_kernel + select_token_kernel: vocab-sharded argmax (lowest index
 //    wins ties).
 #include <cooperative_groups.h>
@@ -182,6 +183,190 @@ __global__ void __launch_bounds__(128) attn_split_kernel(const float* __restrict
   }
 }
 
+// ---------------------------------------------------------------------------
+// Tensor-core split (group G <= 8 q heads per kv head), mma.sync m16n8k16 f16 -> f32.
+// Four warps; warp w owns positions [16w, 16w + 16) of the span.
+//  * scores S[p][h] = K[p] . q[h]: A = the warp's 16 K rows, B = the q heads (N = 8).
+//    The head dimension is permuted the same way in A and B (a dot product does not
+//    depend on the order of its terms): in k-step j, thread (g, t) = (lane / 4, lane % 4)
+//    supplies dims 32t + 4j .. 32t + 4j + 3, so it reads 64 contiguous bytes of each of
+//    its two K rows and of its q head, and no fragment needs a shuffle.  q enters as
+//    q_hi + q_lo (two fp16 terms, ~2^-22 relative), so the fp16 operands add no error
+//    beyond the fp16 cache.
+//  * the span's per-head max and sum of exp through shared memory;
+//  * weighted V: O^T[d][h] = sum_p V[p][d] P[p][h], A = V^T read with ldmatrix.trans from
+//    a shared copy of the span (16-B chunk c of row p stored at chunk c ^ (p & 7), so the
+//    eight rows of an 8x8 matrix fall in different banks), B = P = P_hi + P_lo.
+// The four warps' O^T partials are summed in warp order into the same `partial` record
+// as attn_split_kernel.
+
+__device__ __forceinline__ void mma_f16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                              uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void ldmatrix_x4_trans(uint32_t (&r)[4], const void* smem_row) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_addr(smem_row)));
+}
+
+__device__ __forceinline__ void cp_async_16(void* smem_dst, const void* gmem_src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(smem_dst)),
+               "l"(gmem_src)
+               : "memory");
+}
+
+// (hi, lo) fp16 pairs of two floats: x = hi + lo to ~2^-22 relative.
+__device__ __forceinline__ void split_half2(float x, float y, uint32_t& hi, uint32_t& lo) {
+  const __half2 h = __floats2half2_rn(x, y);
+  const float2 hf = __half22float2(h);
+  const __half2 l = __floats2half2_rn(x - hf.x, y - hf.y);
+  hi = *reinterpret_cast<const uint32_t*>(&h);
+  lo = *reinterpret_cast<const uint32_t*>(&l);
+}
+
+constexpr uint32_t kTcGroup = 8;  // q heads per kv head the tensor-core split handles (<=)
+
+__global__ void __launch_bounds__(128) attn_split_tc_kernel(const float* __restrict__ q,
+                                                            const __half* __restrict__ k_cache,
+                                                            const __half* __restrict__ v_cache,
+                                                            uint32_t G, uint32_t ctx_max,
+                                                            uint32_t ctx_len, uint32_t spans,
+                                                            float* partial) {
+  static_assert(kSpan == 64u, "four warps of 16 positions");
+  __shared__ __align__(128) uint8_t vs[kSpan * kHeadDim * 2u];  // the span's V, swizzled
+  __shared__ float ps[4][16][9];                                 // P per warp [pos][head]
+  __shared__ float ow[4][kTcGroup][kHeadDim + 4u];               // per-warp O^T [head][dim]
+  __shared__ float wmax[4][kTcGroup], wsum[4][kTcGroup];
+  const uint32_t kv = blockIdx.x, span = blockIdx.y, tid = threadIdx.x;
+  const uint32_t lane = tid & 31u, warp = tid >> 5, g = lane >> 2, t = lane & 3u;
+  const uint32_t t0 = span * kSpan;
+  const uint32_t n = ctx_len > t0 ? min(kSpan, ctx_len - t0) : 0u;
+  const float scale = rsqrtf(static_cast<float>(kHeadDim));
+  pdl_wait();  // q and the newest K/V row come from the previous kernel
+  pdl_trigger();
+
+  // V of the span -> shared memory (rows past the context are zero).
+  const __half* vbase = v_cache + (static_cast<size_t>(kv) * ctx_max + t0) * kHeadDim;
+  for (uint32_t i = tid; i < kSpan * 16u; i += 128u) {
+    const uint32_t p = i >> 4, c = i & 15u;
+    uint8_t* dst = vs + p * 256u + ((c ^ (p & 7u)) << 4);
+    if (p < n) {
+      cp_async_16(dst, vbase + p * kHeadDim + c * 8u);
+    } else {
+      *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
+    }
+  }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+
+  // B fragments of the scores: q head g, dims 32t .. 32t + 31 (scaled), as hi + lo.
+  uint32_t qh[8][2], ql[8][2];
+  {
+    const float4* qr = reinterpret_cast<const float4*>(
+        q + (static_cast<size_t>(kv) * G + g) * kHeadDim + 32u * t);
+#pragma unroll
+    for (uint32_t j = 0; j < 8u; ++j) {
+      const float4 v = g < G ? qr[j] : make_float4(0.f, 0.f, 0.f, 0.f);
+      split_half2(v.x * scale, v.y * scale, qh[j][0], ql[j][0]);
+      split_half2(v.z * scale, v.w * scale, qh[j][1], ql[j][1]);
+    }
+  }
+  // A fragments: K rows r0 = 16w + g and r1 = r0 + 8, dims 32t .. 32t + 31.
+  const uint32_t r0 = warp * 16u + g, r1 = r0 + 8u;
+  uint4 ka[4], kb[4];
+  {
+    const uint4* k0 = reinterpret_cast<const uint4*>(
+        k_cache + (static_cast<size_t>(kv) * ctx_max + t0 + r0) * kHeadDim + 32u * t);
+    const uint4* k1 = reinterpret_cast<const uint4*>(
+        k_cache + (static_cast<size_t>(kv) * ctx_max + t0 + r1) * kHeadDim + 32u * t);
+#pragma unroll
+    for (uint32_t c = 0; c < 4u; ++c) {
+      ka[c] = r0 < n ? __ldg(k0 + c) : make_uint4(0u, 0u, 0u, 0u);
+      kb[c] = r1 < n ? __ldg(k1 + c) : make_uint4(0u, 0u, 0u, 0u);
+    }
+  }
+  float sc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (uint32_t j = 0; j < 8u; ++j) {
+    const uint4 x0 = ka[j >> 1], x1 = kb[j >> 1];
+    const uint32_t a[4] = {(j & 1u) ? x0.z : x0.x, (j & 1u) ? x1.z : x1.x,
+                           (j & 1u) ? x0.w : x0.y, (j & 1u) ? x1.w : x1.y};
+    mma_f16_16816(sc, a, qh[j][0], qh[j][1]);
+    mma_f16_16816(sc, a, ql[j][0], ql[j][1]);
+  }
+  // sc = S[r0][2t], S[r0][2t+1], S[r1][2t], S[r1][2t+1]; mask rows past the context
+  if (r0 >= n) sc[0] = sc[1] = -INFINITY;
+  if (r1 >= n) sc[2] = sc[3] = -INFINITY;
+  float m0 = fmaxf(sc[0], sc[2]), m1 = fmaxf(sc[1], sc[3]);
+#pragma unroll
+  for (int off = 4; off < 32; off <<= 1) {
+    m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, off));
+    m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, off));
+  }
+  if (g == 0u) {
+    wmax[warp][2u * t] = m0;
+    wmax[warp][2u * t + 1u] = m1;
+  }
+  __syncthreads();
+  const float mx0 = fmaxf(fmaxf(wmax[0][2u * t], wmax[1][2u * t]), fmaxf(wmax[2][2u * t], wmax[3][2u * t]));
+  const float mx1 = fmaxf(fmaxf(wmax[0][2u * t + 1u], wmax[1][2u * t + 1u]),
+                          fmaxf(wmax[2][2u * t + 1u], wmax[3][2u * t + 1u]));
+  const float e0 = sc[0] == -INFINITY ? 0.f : __expf(sc[0] - mx0);
+  const float e1 = sc[1] == -INFINITY ? 0.f : __expf(sc[1] - mx1);
+  const float e2 = sc[2] == -INFINITY ? 0.f : __expf(sc[2] - mx0);
+  const float e3 = sc[3] == -INFINITY ? 0.f : __expf(sc[3] - mx1);
+  float z0 = e0 + e2, z1 = e1 + e3;
+#pragma unroll
+  for (int off = 4; off < 32; off <<= 1) {
+    z0 += __shfl_xor_sync(0xffffffffu, z0, off);
+    z1 += __shfl_xor_sync(0xffffffffu, z1, off);
+  }
+  if (g == 0u) {
+    wsum[warp][2u * t] = z0;
+    wsum[warp][2u * t + 1u] = z1;
+  }
+  ps[warp][g][2u * t] = e0;
+  ps[warp][g][2u * t + 1u] = e1;
+  ps[warp][g + 8u][2u * t] = e2;
+  ps[warp][g + 8u][2u * t + 1u] = e3;
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+  __syncthreads();  // V in shared memory, P and the sums visible
+  // B fragments of P V: P[pos 2t, 2t+1][head g] and P[pos 2t+8, 2t+9][head g].
+  uint32_t ph0, pl0, ph1, pl1;
+  split_half2(ps[warp][2u * t][g], ps[warp][2u * t + 1u][g], ph0, pl0);
+  split_half2(ps[warp][2u * t + 8u][g], ps[warp][2u * t + 9u][g], ph1, pl1);
+  const uint32_t mi = lane >> 3, rr = lane & 7u;
+  const uint32_t vp = warp * 16u + rr + 8u * (mi >> 1);  // the V row this lane addresses
+#pragma unroll
+  for (uint32_t i = 0; i < 8u; ++i) {
+    const uint32_t chunk = 2u * i + (mi & 1u);
+    uint32_t a[4];
+    ldmatrix_x4_trans(a, vs + vp * 256u + ((chunk ^ (vp & 7u)) << 4));
+    float o[4] = {0.f, 0.f, 0.f, 0.f};
+    mma_f16_16816(o, a, ph0, ph1);
+    mma_f16_16816(o, a, pl0, pl1);
+    // o = O^T[16i + g][2t], [16i + g][2t+1], [16i + g + 8][2t], [16i + g + 8][2t+1]
+    ow[warp][2u * t][16u * i + g] = o[0];
+    ow[warp][2u * t + 1u][16u * i + g] = o[1];
+    ow[warp][2u * t][16u * i + g + 8u] = o[2];
+    ow[warp][2u * t + 1u][16u * i + g + 8u] = o[3];
+  }
+  __syncthreads();
+  for (uint32_t h = 0; h < G; ++h) {
+    float* dst = partial + ((static_cast<size_t>(kv * G + h) * spans) + span) * (kHeadDim + 2u);
+    dst[tid] = ((ow[0][h][tid] + ow[1][h][tid]) + ow[2][h][tid]) + ow[3][h][tid];
+    if (tid == 0u) {
+      dst[kHeadDim] = fmaxf(fmaxf(wmax[0][h], wmax[1][h]), fmaxf(wmax[2][h], wmax[3][h]));
+      dst[kHeadDim + 1u] = ((wsum[0][h] + wsum[1][h]) + wsum[2][h]) + wsum[3][h];
+    }
+  }
+}
+
 // Merge the spans of every q head, normalise, write attn (fp32) and its int8 planes.
 // One CTA of 64 threads (two warps = the head's two 64-column chunks) per q head: the
 // spans' maxima and weights are reduced in parallel, then each thread accumulates its two
@@ -262,6 +447,16 @@ cudaError_t launch_attention(const float* q, const void* k_cache, const void* v_
   const __half* kc = static_cast<const __half*>(k_cache);
   const __half* vc = static_cast<const __half*>(v_cache);
   cudaError_t e;
+  const bool tc = group <= kTcGroup && (reinterpret_cast<uintptr_t>(q) & 15u) == 0u &&
+                  (reinterpret_cast<uintptr_t>(kc) & 15u) == 0u &&
+                  (reinterpret_cast<uintptr_t>(vc) & 15u) == 0u;
+  if (tc) {
+    e = launch_k(attn_split_tc_kernel, grid, 128, 0, stream, q, kc, vc, group, ctx_max, ctx_len,
+                 spans, partial);
+    if (e != cudaSuccess) return e;
+    return launch_k(attn_combine_kernel, n_q, 64, 0, stream, static_cast<const float*>(partial),
+                    spans, used, out, static_cast<ActChunk*>(act));
+  }
   switch (group) {
     case 1: e = launch_k(attn_split_kernel<1>, grid, 128, 0, stream, q, kc, vc, ctx_max, ctx_len, spans, partial); break;
     case 2: e = launch_k(attn_split_kernel<2>, grid, 128, 0, stream, q, kc, vc, ctx_max, ctx_len, spans, partial); break;
