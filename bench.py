@@ -40,10 +40,16 @@ from qgemv_b200 import packs  # noqa: E402
 SWEEP_FORMATS = [packs.Q4K_RAW, packs.Q5K, packs.IQ2S, packs.IQ3S]
 SWEEP_SHAPES = [(4096, 4096), (14336, 4096), (4096, 14336), (128256, 8192)]
 FALLBACK_HBM_GBS = 6650.0
-# DRAM traffic / algorithmic bytes of the GEMV, per format, from one ncu capture each
-# (dram__bytes_read.sum + dram__bytes_write.sum on 32768 x 8192); the roofline's
-# `traffic` is this ratio times the dominant launch's algorithmic bytes.
-TRAFFIC_RATIO = {packs.IQ3S: 1.026, packs.IQ2S: 1.035}
+# DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum, one ncu capture
+# each, `ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum -k regex:gemv_tiled
+# -s 2 -c 1 python bench.py --only F:128256x8192 --steps 3 --warmup 3`) of the sweep's
+# largest GEMVs, one of which is the dominant kernel of the step.
+TRAFFIC_BYTES = {
+    (packs.Q4K_RAW, 128256, 8192): 591090688 + 2896640,
+    (packs.Q5K, 128256, 8192): 722437376 + 3758592,
+    (packs.IQ2S, 128256, 8192): 336776960 + 3912448,
+    (packs.IQ3S, 128256, 8192): 451657728 + 3459072,
+}
 METRIC = "weight-stream GB/s, quant matvec sweep (Q4_K/Q5_K/IQ2_S/IQ3_S x 4 shapes, batch 1)"
 CONFIG = {
     "workload": "BASELINE config 2: batch-1 GEMV sweep {Q4_K,Q5_K,IQ2_S,IQ3_S} x "
@@ -391,7 +397,7 @@ def measure_batched(device, args, peak: float) -> dict:
             "l2": ">= 400 MB of pack copies rotated per replay", "cases": cases}
 
 
-def measure_decode(device, args, world: int, rank: int) -> dict:
+def measure_decode(device, args, world: int, rank: int, layers: int | None = None) -> dict:
     """the 80-layer 70B-class mixed-quant decode step (IQ3_S
     attention, IQ2_S gate/up, Q5_K down, Q4_K vocab head, fp16 KV cache at context
     4096), tensor-parallel over the job's N GPUs, one graph per token.  With N > 1 the
@@ -404,7 +410,7 @@ def measure_decode(device, args, world: int, rank: int) -> dict:
     from qgemv_b200 import decoder
     from qgemv_b200.slice import StepGraph
 
-    spec = decoder.ModelSpec()
+    spec = decoder.ModelSpec() if layers is None else decoder.ModelSpec(layers=layers)
     w = decoder.synthetic_rank_weights(spec, rank, world, device, seed=1)
     x = torch.randn(spec.hidden, device=device)
     pos = spec.ctx_max - 1
@@ -456,7 +462,7 @@ def measure_decode(device, args, world: int, rank: int) -> dict:
     del w
     torch.cuda.empty_cache()
     moved = spec.weight_bytes() + spec.kv_bytes_read(spec.ctx_max)
-    return {"workload": "BASELINE config 5: 80-layer 70B-class decode step, ctx 4096, batch 1",
+    return {"workload": f"BASELINE config 5: {spec.layers}-layer 70B-class decode step, ctx 4096, batch 1",
             "tp": world, "ms_per_token": ms, "tok_per_s": 1000.0 / ms,
             "collective": "fused NVLink exchange in the Wo/Wd GEMVs" if world > 1 else None,
             "weight_bytes": spec.weight_bytes(), "kv_bytes": spec.kv_bytes_read(spec.ctx_max),
@@ -478,6 +484,16 @@ def run_ours(args) -> int:
     if world > 1:
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+
+    if args.only and args.only.startswith("decode:"):
+        # profiling case: the decode step alone with the given number of layers
+        stats = measure_decode(device, args, world, rank, layers=int(args.only.split(":")[1]))
+        if rank == 0:
+            print(json.dumps({"profiling_case": args.only, "decode": stats}))
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return 0
 
     # Resident packs + activations (setup, untimed).
     mats = []
@@ -578,15 +594,35 @@ def run_ours(args) -> int:
     peak, peak_src = measured_peak()
     dom = max(range(len(mats)), key=lambda i: per[i]["ms"])
     dm = mats[dom]
-    ratio = TRAFFIC_RATIO.get(dm["fmt"])
+    traffic = TRAFFIC_BYTES.get((dm["fmt"], dm["rows"], dm["cols"]))
+    # The dominant GEMV alone: R launches back to back in one graph (its weights exceed
+    # L2, so every launch streams them from HBM), CUDA events on the launching stream.
+    R = 8
+    chain = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(chain):
+        for _ in range(R):
+            launch(dm, xs[dm["cols"]], acts[dm["cols"]])
+    prewarm(chain.replay, torch.cuda.synchronize, seconds=0.2)
+    c0 = torch.cuda.Event(enable_timing=True)
+    c1 = torch.cuda.Event(enable_timing=True)
+    c0.record()
+    for _ in range(args.steps):
+        chain.replay()
+    c1.record()
+    torch.cuda.synchronize()
+    dom_ms = c0.elapsed_time(c1) / (args.steps * R)
+    del chain
+    dom_gbps = dm["bytes"] / (dom_ms * 1e-3) / 1e9
     roofline = {
         "bound": "hbm", "kernel": f"gemv_tiled_kernel<{packs.FORMAT_NAMES[dm['fmt']]}> {dm['rows']}x{dm['cols']}",
-        "achieved": per[dom]["GBps"], "peak": peak, "unit": "GB/s",
-        "frac": per[dom]["GBps"] / peak, "peak_source": peak_src,
+        "achieved": dom_gbps, "peak": peak, "unit": "GB/s",
+        "frac": dom_gbps / peak, "peak_source": peak_src,
+        "launch_us": dom_ms * 1e3,
+        "timing": f"{R} back-to-back launches of this GEMV in one graph, CUDA events, {args.steps} replays",
         "algorithmic_bytes_per_launch": dm["bytes"],
-        "traffic": None if ratio is None else round(ratio * dm["bytes"]),
-        "traffic_source": None if ratio is None else
-        "ncu dram__bytes_read.sum + dram__bytes_write.sum of the same kernel at 32768 rows, scaled by rows",
+        "traffic": traffic,
+        "traffic_source": None if traffic is None else
+        "ncu dram__bytes_read.sum + dram__bytes_write.sum of the same kernel and shape (bench.py --only)",
     }
     for row in per:
         row["frac_of_peak"] = row["GBps"] / peak
@@ -668,7 +704,8 @@ def main() -> int:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--only", default=None,
                     help="profiling case: run a single GEMV FMT:ROWSxCOLS (e.g. 0:32768x8192) "
-                         "instead of the sweep; skips the CPU baseline")
+                         "instead of the sweep, or decode:LAYERS (the decode step alone with "
+                         "that many layers); skips the CPU baseline")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
