@@ -302,8 +302,12 @@ __global__ void __launch_bounds__(1024) gather_norm_prepare_kernel(
     if (threadIdx.x == 0u) part = sq;
   }
   cluster.sync();  // every CTA's partial sum of squares is in its shared memory
+  float pc[8];
+#pragma unroll
+  for (uint32_t c = 0; c < 8u; ++c) pc[c] = c < ncta ? *cluster.map_shared_rank(&part, c) : 0.f;
   float total = 0.f;
-  for (uint32_t c = 0; c < ncta; ++c) total += *cluster.map_shared_rank(&part, c);
+#pragma unroll
+  for (uint32_t c = 0; c < 8u; ++c) total += pc[c];  // CTA order (the unused slots add 0)
   const float inv = 1.0f / sqrtf(total / static_cast<float>(n) + eps);
   const uint32_t lane = threadIdx.x & 31u;
   const float* xv = nsrc != 0u ? x_out : x_in;
@@ -354,10 +358,59 @@ cudaError_t launch_gather_norm_prepare(const uint64_t* buf, uint32_t* epoch, uin
 }
 
 // h = x / sqrt(mean(x^2) + eps) * w and h's int8 planes (the layer slice's and the
-// decoder's RMSNorm; the same cluster kernel reading x directly).
+// decoder's RMSNorm when there is nothing to gather).  No cluster: every CTA sums the
+// squares of the whole vector itself (it was just written, so it is read from L2), with
+// the same loads and the same reduction order in every CTA, so all CTAs hold the same
+// bits; then each normalises and prepares its own 64-column chunks, one warp per chunk.
+constexpr uint32_t kNormThreads = 256;
+
+__global__ void __launch_bounds__(kNormThreads) norm_prepare_kernel(const float* __restrict__ x,
+                                                                    const float* __restrict__ w,
+                                                                    uint32_t n, float eps, float* h,
+                                                                    ActChunk* act) {
+  __shared__ float ws[kNormThreads / 32u];
+  pdl_wait();
+  pdl_trigger();
+  float sq = 0.f;
+  if ((reinterpret_cast<uintptr_t>(x) & 15u) == 0u) {
+    const float4* x4 = reinterpret_cast<const float4*>(x);
+#pragma unroll 4
+    for (uint32_t i = threadIdx.x; i < n / 4u; i += kNormThreads) {
+      const float4 v = x4[i];
+      sq = fmaf(v.x, v.x, sq);
+      sq = fmaf(v.y, v.y, sq);
+      sq = fmaf(v.z, v.z, sq);
+      sq = fmaf(v.w, v.w, sq);
+    }
+  } else {
+    for (uint32_t i = threadIdx.x; i < n; i += kNormThreads) sq = fmaf(x[i], x[i], sq);
+  }
+  for (int off = 16; off > 0; off >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, off);
+  const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
+  if (lane == 0u) ws[warp] = sq;
+  __syncthreads();
+  float total = 0.f;
+#pragma unroll
+  for (uint32_t k = 0; k < kNormThreads / 32u; ++k) total += ws[k];
+  const float inv = 1.0f / sqrtf(total / static_cast<float>(n) + eps);
+  const uint32_t c = blockIdx.x * (kNormThreads / 32u) + warp;
+  if (c < n / 64u) {
+    const uint32_t i = 64u * c + 2u * lane;
+    const float v0 = x[i] * inv * w[i], v1 = x[i + 1u] * inv * w[i + 1u];
+    if (h != nullptr) {
+      h[i] = v0;
+      h[i + 1u] = v1;
+    }
+    warp_prepare_chunk(v0, v1, act + c);
+  }
+}
+
 cudaError_t launch_norm_prepare(const float* x, const float* w, uint32_t n, float eps, float* h,
                                 void* act, cudaStream_t stream) {
-  return launch_cluster_norm(nullptr, nullptr, 0u, 0u, x, w, n, eps, nullptr, h, act, stream);
+  if (n == 0u || n % 64u != 0u) return cudaErrorInvalidValue;
+  const uint32_t chunks = n / 64u, per = kNormThreads / 32u;
+  return launch_k(norm_prepare_kernel, (chunks + per - 1u) / per, kNormThreads, 0, stream, x, w, n,
+                  eps, h, static_cast<ActChunk*>(act));
 }
 
 // a = silu(gate) * up fused with a's activation preparation (one warp per 64 columns;
