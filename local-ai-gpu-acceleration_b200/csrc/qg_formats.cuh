@@ -315,9 +315,24 @@ __device__ __forceinline__ void q4_nibble_dot(const uint4 q0, const uint4 q1, co
 #define QG_IQ2S_KGRID_COPIES 8u
 #endif
 constexpr uint32_t kIq2Copies = QG_IQ2S_KGRID_COPIES;
-static_assert(kIq2Copies == 4u || kIq2Copies == 8u, "IQ2_S grid copies: 4 or 8");
+static_assert(kIq2Copies == 4u || kIq2Copies == 8u || kIq2Copies == 16u,
+              "IQ2_S grid copies: 4, 8 or 16");
+// IQ2_S sign masks: from the shared table (0) or computed in registers (1, no table).
+#ifndef QG_IQ2S_ALU_SIGNS
+#define QG_IQ2S_ALU_SIGNS 1
+#endif
+constexpr bool kIq2AluSigns = QG_IQ2S_ALU_SIGNS != 0;
 constexpr uint32_t kIq2SignWord = 2048u * kIq2Copies;  // word offset of the IQ2_S sign table
-constexpr uint32_t kIq2TableBytes = (kIq2SignWord + 8192u) * 4u;
+constexpr uint32_t kIq2TableBytes = (kIq2SignWord + (kIq2AluSigns ? 0u : 8192u)) * 4u;
+
+// Byte masks of four sign bits: byte i = 0xFF where bit i of s4 (< 16) is set.  The
+// multiply puts bit i at bit 8i + 7 (its four partial products do not overlap, so no
+// carries), and prmt's sign-replicating selector copies each byte's top bit over it.
+__device__ __forceinline__ uint32_t sign_bytes4(uint32_t s4) {
+  uint32_t m;
+  asm("prmt.b32 %0, %1, 0, 0xBA98;" : "=r"(m) : "r"(s4 * 0x10204080u));
+  return m;
+}
 #ifndef QG_IQ3S_GRID_COPIES
 #define QG_IQ3S_GRID_COPIES 32u
 #endif
@@ -471,9 +486,17 @@ __device__ __forceinline__ float chunk_dot<QG_FMT_IQ2S>(const uint8_t* rp, const
     for (int g = 0; g < 4; ++g) {
       const uint32_t idx = byte_of(gl[ib], g) | ((qhb << (8 - 2 * g)) & 0x300u);
       const uint2 k2 = t.kgrid2[idx * kIq2Copies];
-      const uint2 sm = t.sign2[byte_of(sg[ib], g) << 4];
-      const uint32_t u0 = k2.x ^ sm.x ^ 0x09090909u;
-      const uint32_t u1 = k2.y ^ sm.y ^ 0x09090909u;
+      uint32_t u0, u1;
+      if constexpr (kIq2AluSigns) {
+        // table bytes are 2k ^ 9; a set sign bit flips them with 0x0E (2k ^ 7)
+        const uint32_t sb = byte_of(sg[ib], g);
+        u0 = k2.x ^ (sign_bytes4(sb & 0x0fu) & 0x0e0e0e0eu);
+        u1 = k2.y ^ (sign_bytes4(sb >> 4) & 0x0e0e0e0eu);
+      } else {
+        const uint2 sm = t.sign2[byte_of(sg[ib], g) << 4];
+        u0 = k2.x ^ sm.x ^ 0x09090909u;
+        u1 = k2.y ^ sm.y ^ 0x09090909u;
+      }
       ih[g >> 1] = dp4a(u1, H[2 * g + 1], dp4a(u0, H[2 * g], ih[g >> 1]));
       il[g >> 1] = dp4a(u1, Lp[2 * g + 1], dp4a(u0, Lp[2 * g], il[g >> 1]));
     }
@@ -566,11 +589,11 @@ constexpr ReplicatedTables make_iq2s() {
     }
     for (uint32_t r = 0; r < kIq2Copies; ++r) {
       const uint32_t slot = kIq2Copies * e + r;
-      t.w[2u * slot] = lo;
-      t.w[2u * slot + 1u] = hi;
+      t.w[2u * slot] = kIq2AluSigns ? lo ^ 0x09090909u : lo;
+      t.w[2u * slot + 1u] = kIq2AluSigns ? hi ^ 0x09090909u : hi;
     }
   }
-  put_sign_copies(t, kIq2SignWord, 0x0eu);
+  if (!kIq2AluSigns) put_sign_copies(t, kIq2SignWord, 0x0eu);
   return t;
 }
 

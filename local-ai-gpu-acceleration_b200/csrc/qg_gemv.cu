@@ -776,15 +776,16 @@ uint32_t ctas_per_sm(const GemvPlan& p) {
 // Passes per tile.  Tiles go round-robin to the G = min(T, slots) persistent CTAs, so
 // CTA j runs ceil(T / G) or one fewer tiles, and an SM runs whichever m CTAs the block
 // scheduler put on it (m = CTAs per SM when G exceeds the SM count, else 1).  Cost of
-// a tile size P (a multiple of the stage's q passes, at most 128): the tiles of the m
+// a tile size P (a multiple of the stage's q passes, at most p_max): the tiles of the m
 // busiest CTAs times (P + 1/2) -- the half pass stands for a tile's barrier and
 // epilogue -- divided by 0.6 when a CTA sized to share its SM runs alone (measured on
 // B200: one 9-warp CTA streams ~0.6 of what two do).  Ties go to the larger P.
-uint32_t balanced_passes(uint32_t total_passes, uint32_t q, uint32_t sms, uint32_t cps) {
+uint32_t balanced_passes(uint32_t total_passes, uint32_t q, uint32_t sms, uint32_t cps,
+                         uint32_t p_max) {
   const uint32_t slots = sms * cps;
   uint32_t best_p = q;
   double best_cost = 1e300;
-  for (uint32_t P = q; P <= std::max(q, 128u); P += q) {
+  for (uint32_t P = q; P <= std::max(q, p_max); P += q) {
     const uint32_t T = (total_passes + P - 1u) / P;
     const uint32_t G = std::min(T, slots);
     const uint32_t k = (T + G - 1u) / G;         // tiles of the busiest CTAs
@@ -834,15 +835,17 @@ GemvPlan plan_gemv(int fmt, uint32_t rows, uint32_t cols, int sms) {
   // Small matrices: a stage is never more passes than the matrix has (but never less
   // than its 16-B aligned size).
   while (q > q_align && q > total_passes) q >>= 1;
-  // Two stages of q passes, the codebooks and a worst-case reduction buffer must fit the
-  // 227 KB a CTA may opt into (else the launch would drop to the all-thread kernels).
-  auto fits = [&](uint32_t qq) {
-    const uint32_t stage = ((qq * p.rpp * row_bytes + 127u) & ~127u) +
-                           ((qq * p.rpp * row_meta + 127u) & ~127u);
-    const uint32_t red = 2u * 128u * p.rpp * (tpr / p.group) * 4u;
-    return 2u * stage + red + iq_table_bytes(fmt) + 1024u <= kSmemOptinMax;
+  // Two stages of q passes, the codebooks and the reduction buffer of tiles of at least
+  // 16 passes must fit the 227 KB a CTA may opt into (else the launch would drop to the
+  // all-thread kernels); the tile size is then capped by what is left.
+  const uint32_t red_per_pass = 2u * p.rpp * (tpr / p.group) * 4u;  // double-buffered floats
+  auto stage_of = [&](uint32_t qq) {
+    return ((qq * p.rpp * row_bytes + 127u) & ~127u) + ((qq * p.rpp * row_meta + 127u) & ~127u);
   };
-  while (q > q_align && !fits(q)) q >>= 1;
+  auto fixed_of = [&](uint32_t qq) { return 2u * stage_of(qq) + iq_table_bytes(fmt) + 1024u; };
+  while (q > q_align && fixed_of(q) + 16u * red_per_pass > kSmemOptinMax) q >>= 1;
+  const uint32_t p_max =
+      fixed_of(q) < kSmemOptinMax ? std::min(128u, (kSmemOptinMax - fixed_of(q)) / red_per_pass) : q;
   p.stage_passes = q;
   p.stage_rows = q * p.rpp;
   const uint32_t pay = p.stage_rows * row_bytes, met = p.stage_rows * row_meta;
@@ -856,7 +859,8 @@ GemvPlan plan_gemv(int fmt, uint32_t rows, uint32_t cols, int sms) {
   p.rows_per_tile = q * p.rpp;
   plan_smem(fmt, tpr, p);
   const uint32_t cps = ctas_per_sm(p);
-  const uint32_t P = balanced_passes(total_passes, q, static_cast<uint32_t>(sms), cps);
+  const uint32_t P = balanced_passes(total_passes, q, static_cast<uint32_t>(sms), cps,
+                                     std::max(q, p_max - p_max % q));
   p.passes = P;
   p.rows_per_tile = P * p.rpp;
   p.num_tiles = (rows + p.rows_per_tile - 1u) / p.rows_per_tile;
