@@ -126,8 +126,11 @@ def test_rows_limit_caps_launched_rows(cuda, port):
     assert_rows_close(yc[:9], want, row_tol(port, packs.IQ3S, pk.payload, None, x, 40, 1024)[:9])
 
 
+# (5, 8192), (6, 4096), (9, 8192): two or three row passes in all, so the planner shrinks
+# the four-pass stage to two (the two-row transposed reduction); (250, 2048): one warp
+# per row, four-pass stages, a partial last tile.
 SHAPES = [(1, 256), (5, 768), (37, 1792), (64, 3584), (33, 14336), (130, 4096), (17, 28672),
-          (3, 33024), (1000, 1024)]
+          (3, 33024), (1000, 1024), (5, 8192), (6, 4096), (9, 8192), (250, 2048)]
 
 
 @pytest.mark.parametrize("fmt", list(FORMAT_TAGS))
