@@ -16,6 +16,9 @@ pytestmark = pytest.mark.gpu
 
 SMALL = dict(layers=2, hidden=512, n_q_heads=4, n_kv_heads=2, head_dim=128, ffn=1024,
              vocab=1000, ctx_max=64)
+# a model that shards four ways (every rank: 2 q heads, 1 kv head, 512 ffn rows, 256 vocab rows)
+SMALL_TP4 = dict(layers=2, hidden=1024, n_q_heads=8, n_kv_heads=4, head_dim=128, ffn=2048,
+                 vocab=1024, ctx_max=64)
 
 
 def _oracle(port, model, x, pos):
@@ -92,7 +95,7 @@ def test_decoder_graph_replay_matches_eager(cuda):
 TP_STEPS = (30, 31, 32)  # positions; the middle step runs as a captured graph
 
 
-def _tp_rank(rank, world, q_in, q_out):
+def _tp_rank(rank, world, q_in, q_out, spec_kw):
     sys.path.insert(0, str(REPO / "local-ai-gpu-acceleration_b200"))
     import torch
 
@@ -100,7 +103,7 @@ def _tp_rank(rank, world, q_in, q_out):
     from qgemv_b200.slice import StepGraph
 
     torch.cuda.set_device(rank)
-    spec = decoder.ModelSpec(**SMALL)
+    spec = decoder.ModelSpec(**spec_kw)
     model = decoder.HostModel.synthetic(spec, seed=21)
     if rank == 0:
         nid = decoder.nccl_unique_id()
@@ -130,17 +133,18 @@ def _tp_rank(rank, world, q_in, q_out):
     dec.close()
 
 
-@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
-                    reason="needs 2 GPUs")
-def test_decoder_tp2_matches_oracle(port):
-    """Two ranks over NVLink (fused exchange in the Wo / Wd GEMVs, NCCL only for the
+@pytest.mark.parametrize("world,spec_kw", [(2, SMALL), (4, SMALL_TP4)], ids=["tp2", "tp4"])
+def test_decoder_tp_matches_oracle(port, world, spec_kw):
+    """World ranks over NVLink (fused exchange in the Wo / Wd GEMVs, NCCL only for the
     token all-gather): three consecutive steps -- eager, captured graph, eager -- against
     the oracle stepping the same model with its caches carried along."""
+    if not torch.cuda.is_available() or torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     sys.path.insert(0, str(REPO / "oracle"))
     import decode_oracle
     from qgemv_b200 import decoder, packs
 
-    spec = decoder.ModelSpec(**SMALL)
+    spec = decoder.ModelSpec(**spec_kw)
     model = decoder.HostModel.synthetic(spec, seed=21)
     w = copy.deepcopy(decoder.rank_weights(model, 0, 1))
     want = []
@@ -150,7 +154,7 @@ def test_decoder_tp2_matches_oracle(port):
     ctx = mp.get_context("spawn")
     q_in, q_out = ctx.Queue(), ctx.Queue()
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
-    procs = [ctx.Process(target=_tp_rank, args=(r, 2, q_in, q_out)) for r in range(2)]
+    procs = [ctx.Process(target=_tp_rank, args=(r, world, q_in, q_out, spec_kw)) for r in range(world)]
     for p in procs:
         p.start()
     res = [q_out.get(timeout=300) for _ in procs]
@@ -161,5 +165,6 @@ def test_decoder_tp2_matches_oracle(port):
         for (tok, hid), (want_tok, want_hidden) in zip(steps, want):
             _check(hid, want_hidden, tok, want_tok)
     # every rank holds the same bits of the replicated hidden state
-    for (_, a), (_, b) in zip(res[0][1], res[1][1]):
-        assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+    for _, other in res[1:]:
+        for (_, a), (_, b) in zip(res[0][1], other):
+            assert np.array_equal(a.view(np.uint32), b.view(np.uint32))

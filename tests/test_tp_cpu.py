@@ -1,4 +1,4 @@
-"""Tensor-parallel sharding arithmetic on CPU ranks (gloo, world size 2): each rank runs
+"""Tensor-parallel sharding arithmetic on CPU ranks (gloo, world size 2 and 4): each rank runs
 the oracle decode step on its own shards (row shards of Wq/Wk/Wv/Wg/Wu/head, column
 shards of Wo/Wd, its kv heads), with the residual on rank 0 and real gloo all-reduce /
 all-gather, and must reproduce the single-rank step."""
@@ -14,10 +14,13 @@ from conftest import REPO
 
 SPEC_KW = dict(layers=2, hidden=512, n_q_heads=4, n_kv_heads=2, head_dim=128, ffn=1024,
                vocab=1000, ctx_max=64)
+# shards four ways: every rank 2 q heads, 1 kv head, 512 ffn rows, 256 vocab rows
+SPEC_KW_TP4 = dict(layers=2, hidden=1024, n_q_heads=8, n_kv_heads=4, head_dim=128, ffn=2048,
+                   vocab=1024, ctx_max=64)
 POS = 37
 
 
-def _rank_main(rank, world, port_no, q):
+def _rank_main(rank, world, port_no, q, spec_kw):
     sys.path.insert(0, str(REPO / "local-ai-gpu-acceleration_b200"))
     sys.path.insert(0, str(REPO / "oracle"))
     import torch
@@ -30,7 +33,7 @@ def _rank_main(rank, world, port_no, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port_no))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
-        spec = decoder.ModelSpec(**SPEC_KW)
+        spec = decoder.ModelSpec(**spec_kw)
         model = decoder.HostModel.synthetic(spec, seed=4)
         w = decoder.rank_weights(model, rank, world)
         x = packs.synthetic_activation(spec.hidden, 5)
@@ -52,12 +55,13 @@ def _rank_main(rank, world, port_no, q):
         dist.destroy_process_group()
 
 
-def test_tp2_sharding_matches_single_rank(port):
+@pytest.mark.parametrize("world,spec_kw", [(2, SPEC_KW), (4, SPEC_KW_TP4)], ids=["tp2", "tp4"])
+def test_tp_sharding_matches_single_rank(port, world, spec_kw):
     sys.path.insert(0, str(REPO / "oracle"))
     import decode_oracle
     from qgemv_b200 import decoder, packs
 
-    spec = decoder.ModelSpec(**SPEC_KW)
+    spec = decoder.ModelSpec(**spec_kw)
     model = decoder.HostModel.synthetic(spec, seed=4)
     x = packs.synthetic_activation(spec.hidden, 5)
     tok1, hid1 = decode_oracle.step(port, spec, decoder.rank_weights(model, 0, 1), x, POS)
@@ -65,7 +69,8 @@ def test_tp2_sharding_matches_single_rank(port):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port_no = 29500 + os.getpid() % 1000
-    procs = [ctx.Process(target=_rank_main, args=(r, 2, port_no, q)) for r in range(2)]
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port_no + world, q, spec_kw))
+             for r in range(world)]
     for p in procs:
         p.start()
     res = [q.get(timeout=300) for _ in procs]
