@@ -1,6 +1,7 @@
 """Generate tests/golden/*.npz from the reference's own code.
 
-Run in a container that has the reference tree (default /root/reference):
+Run where the reference tree is present (its root as the argument, else the default
+root that oracle/qoracle.py uses):
 
     python tests/golden/make_golden.py [reference_root]
 
