@@ -10,14 +10,18 @@
 //    barrier.
 //  * Consumer thread (slot, c) owns the 64-column chunk c: its x values are loaded
 //    once, as two int8 planes, and every row's chunk is a string of dp4a
-//    instructions (qg_formats.cuh).  Row sums: shuffle reduction in lane groups of
-//    gcd(cols/64, 32) (for full-warp groups and stages of 4k passes, four rows at a
-//    time with one transposed butterfly), shared-memory partials, one consumer
-//    barrier per tile, then the epilogue (y, optional residual, the reference's KV
-//    page word).
+//    instructions (qg_formats.cuh).  Stages hold four passes where the shape allows
+//    (fewer for matrices of two or three passes), so a thread has four independent
+//    rows per stage wait.  Row sums: with full-warp lane groups (cols/64 a multiple
+//    of 32) four (or two) rows at a time with one transposed butterfly, otherwise a
+//    shuffle reduction in lane groups of gcd(cols/64, 32); shared-memory partials,
+//    one consumer barrier per tile, then the epilogue (y, optional residual, the
+//    reference's KV page word, optional peer stores of the tensor-parallel exchange).
+//  * Tile size (passes per tile) chosen per shape so the tiles spread evenly over the
+//    SMs (balanced_passes), capped by the shared memory left after stages and tables.
 //  * IQ formats (issue- and shared-memory-bound, not HBM-bound): 16 consumer warps,
-//    one CTA per SM, stages of four passes, codebooks replicated in shared memory
-//    so that table lookups spread over the banks (qg_formats.cuh).
+//    one CTA per SM, codebooks replicated in shared memory so that table lookups
+//    spread over the banks; IQ2_S sign masks computed in registers (qg_formats.cuh).
 //  * Every mbarrier wait is bounded (QG_ERR_WAIT_TIMEOUT); the producer waits for its
 //    copies in flight before it exits.
 // gemv_staged_kernel<FMT> handles packs whose base address is not 16-B aligned
