@@ -324,7 +324,7 @@ BATCHED_SHAPES = [(28672, 8192), (8192, 28672)]
 BATCHED_SIZES = [1, 8, 16, 32]
 
 
-def measure_batched(device, args, peak: float) -> dict:
+def measure_batched(device, args, peak: float, only: tuple | None = None) -> dict:
     """{Q4_K, IQ2_S} x {28672x8192, 8192x28672} at batch 1, 8, 16, 32.
     Batch 1 is the GEMV (qg_act_prepare + qg_gemv_act); batch >= 2 is qg_gemm_batched
     (tensor cores).  Each graph replay walks a rotation of pack copies totalling >= 400 MB,
@@ -335,15 +335,18 @@ def measure_batched(device, args, peak: float) -> dict:
 
     stream = torch.cuda.Stream(device)
     cases = []
-    for fmt in BATCHED_FORMATS:
-        for rows, cols in BATCHED_SHAPES:
+    formats, shapes, sizes = BATCHED_FORMATS, BATCHED_SHAPES, BATCHED_SIZES
+    if only is not None:  # profiling case: one (format, rows, cols, batch)
+        formats, shapes, sizes = [only[0]], [(only[1], only[2])], [only[3]]
+    for fmt in formats:
+        for rows, cols in shapes:
             pk = packs.synthetic_pack(fmt, rows, cols, seed=rows ^ cols ^ fmt)
             nbytes = packs.pack_bytes(fmt, rows, cols)
             copies = max(2, -(-400_000_000 // nbytes))
             base = torch.from_numpy(pk.payload).to(device)
             payloads = [base] + [base.clone() for _ in range(copies - 1)]
             del pk
-            for batch in BATCHED_SIZES:
+            for batch in sizes:
                 x = torch.randn(batch, cols, device=device)
                 y = torch.empty(batch, rows, device=device)
                 if batch == 1:
@@ -485,6 +488,15 @@ def run_ours(args) -> int:
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
 
+    if args.only and args.only.startswith("batched:"):
+        # profiling case: one batched GEMM, batched:FMT:ROWSxCOLS:BATCH
+        _, f, shape, b = args.only.split(":")
+        r, c = shape.lower().split("x")
+        peak, _ = measured_peak()
+        stats = measure_batched(device, args, peak, only=(int(f), int(r), int(c), int(b)))
+        if rank == 0:
+            print(json.dumps({"profiling_case": args.only, "batched": stats}))
+        return 0
     if args.only and args.only.startswith("decode:"):
         # profiling case: the decode step alone with the given number of layers
         stats = measure_decode(device, args, world, rank, layers=int(args.only.split(":")[1]))
@@ -726,8 +738,9 @@ def main() -> int:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--only", default=None,
                     help="profiling case: run a single GEMV FMT:ROWSxCOLS (e.g. 0:32768x8192) "
-                         "instead of the sweep, or decode:LAYERS (the decode step alone with "
-                         "that many layers); skips the CPU baseline")
+                         "instead of the sweep, decode:LAYERS (the decode step alone with "
+                         "that many layers) or batched:FMT:ROWSxCOLS:BATCH (one config-4 case); "
+                         "skips the CPU baseline")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
