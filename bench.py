@@ -41,8 +41,8 @@ SWEEP_FORMATS = [packs.Q4K_RAW, packs.Q5K, packs.IQ2S, packs.IQ3S]
 SWEEP_SHAPES = [(4096, 4096), (14336, 4096), (4096, 14336), (128256, 8192)]
 FALLBACK_HBM_GBS = 6650.0
 # DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum, one ncu capture
-# each, `ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum -k regex:gemv_tiled
-# -s 2 -c 1 python bench.py --only F:128256x8192 --steps 3 --warmup 3`) of the sweep's
+# each, `ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum --clock-control none
+# -k regex:gemv_tiled -s 2 -c 1 python bench.py --only F:128256x8192 --steps 3 --warmup 3`) of the sweep's
 # largest GEMVs, one of which is the dominant kernel of the step.
 TRAFFIC_BYTES = {
     (packs.Q4K_RAW, 128256, 8192): 591090688 + 2896640,

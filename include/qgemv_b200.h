@@ -267,8 +267,8 @@ cudaError_t qg_argmax_token(const float* values, uint32_t n, uint32_t* token,
  * with tcgen05.mma (M=128, N=16 or 32) against x scaled by a power of two per batch row
  * and rounded to fp16; |error| <= 2^-11 * ||w_row||_1 * ||x_b||_inf.  Results are
  * deterministic.  Three launches on `stream`; `workspace` (256-B aligned, caller-owned) holds the
- * prepared x and the split-row partial sums: qg_gemm_batched_workspace_bytes, queried
- * with the device current that will run the call (it depends on the SM count). */
+ * prepared x and the split-row partial sums: qg_gemm_batched_workspace_bytes (sized for
+ * grids of up to 256 CTAs, so the size does not depend on the device it is queried on). */
 cudaError_t qg_gemm_batched_workspace_bytes(int fmt, uint32_t batch, uint32_t rows, uint32_t cols,
                                             size_t* bytes);
 cudaError_t qg_gemm_batched(int fmt, const uint8_t* payload, const uint8_t* meta, const float* x,
@@ -324,8 +324,10 @@ cudaError_t qg_layer_slice_forward(const qg_layer_slice* s, const float* x, floa
  * per device (enough for hidden 8192 / ffn 28672); nothing is allocated or freed.
  *  - Returns cudaErrorInvalidValue when qg_layer_slice_workspace_bytes(s) exceeds
  *    QG_SLICE_STATIC_SCRATCH_BYTES (use qg_layer_slice_forward with a workspace).
- *  - The first call on each device (that device current) looks up the array's device
- *    address once (cudaGetSymbolAddress); make that first call before any stream capture.
+ *  - The array's device address belongs to one CUDA context.  The first call in each
+ *    context (the first on each device, the first after cudaDeviceReset, the first
+ *    under another driver-API context) looks it up (cudaGetSymbolAddress) and caches
+ *    it with the context's id; make that first call before any stream capture.
  *  - One array per device: calls whose work overlaps on a device (different streams
  *    or host threads) race on it; serialise them on one stream. */
 #define QG_SLICE_STATIC_SCRATCH_BYTES (1u << 20)

@@ -1025,8 +1025,14 @@ bool tc_format(int fmt) {
   return fmt == QG_FMT_Q4K_RAW || fmt == QG_FMT_Q5K || fmt == QG_FMT_IQ2S || fmt == QG_FMT_IQ3S;
 }
 
+// Partial-sum slots in the workspace: one pair per CTA of a grid of at most kMaxTcGrid
+// CTAs, so the workspace size does not depend on the device the size was queried on
+// (the launch grid is min(units, SMs, kMaxTcGrid)).
+constexpr uint32_t kMaxTcGrid = 256u;
+
 uint32_t grid_for(uint32_t sms, uint64_t units) {
-  return units < sms ? static_cast<uint32_t>(units) : sms;
+  const uint32_t cap = sms < kMaxTcGrid ? sms : kMaxTcGrid;
+  return units < cap ? static_cast<uint32_t>(units) : cap;
 }
 
 std::mutex g_attr_mutex;
@@ -1104,12 +1110,10 @@ bool encode_payload_map(CUtensorMap* map, const uint8_t* payload, uint32_t rows,
 
 uint32_t gemm_tc_nb(uint32_t batch) { return batch <= 16u ? 16u : 32u; }
 
+// Independent of the current device (no CUDA call): sized for the largest grid.
 cudaError_t gemm_tc_workspace_bytes(uint32_t batch, uint32_t rows, uint32_t cols, size_t* bytes) {
-  int sms = 0;
-  cudaError_t e = sm_count(&sms);
-  if (e != cudaSuccess) return e;
   const uint64_t units = static_cast<uint64_t>((rows + kTileM - 1u) / kTileM) * (cols / kBlockCols);
-  *bytes = tc_workspace(gemm_tc_nb(batch), rows, cols, grid_for(static_cast<uint32_t>(sms), units)).total;
+  *bytes = tc_workspace(gemm_tc_nb(batch), rows, cols, grid_for(kMaxTcGrid, units)).total;
   return cudaSuccess;
 }
 
@@ -1124,7 +1128,7 @@ cudaError_t launch_gemm_tc(int fmt, const uint8_t* payload, const float* x, floa
   const uint32_t tiles = (rows + kTileM - 1u) / kTileM;
   const uint64_t units = static_cast<uint64_t>(tiles) * kb;
   const uint32_t grid = grid_for(static_cast<uint32_t>(sms), units);
-  const TcWorkspace w = tc_workspace(nb, rows, cols, grid);
+  const TcWorkspace w = tc_workspace(nb, rows, cols, grid_for(kMaxTcGrid, units));
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   TcArgs a{};
   a.payload = payload;

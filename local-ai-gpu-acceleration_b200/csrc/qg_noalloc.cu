@@ -11,10 +11,15 @@
 // For them the scratch is linked into the library: QG_SLICE_STATIC_SCRATCH_BYTES per
 // device, reserved when the module loads, never allocated or freed by this code.
 //
-// Set-up: the first call on each device (with that device current) looks up the
-// array's device address with cudaGetSymbolAddress and caches it.  That lookup may
-// load the module, so the first call on a device should come before any stream
-// capture.  Later calls do no CUDA API work besides the slice's own launches.
+// Set-up: a device address of the array is only valid in the CUDA context that was
+// current when it was looked up.  Each call reads the current context's process-unique
+// id (cuCtxGetCurrent + cuCtxGetId, through the runtime's driver entry points, so the
+// library does not link libcuda itself); the first call in a context (the first on
+// each device, and the first after cudaDeviceReset or under a different driver-API
+// context) looks the address up with cudaGetSymbolAddress and caches it beside that id.
+// That lookup may load the module, so the first call in a context should come before
+// any stream capture.  Later calls in the same context do no CUDA API work besides the
+// id query and the slice's own launches.
 //
 // Nothing in the scratch needs to start at zero: every intermediate vector and every
 // activation plane buffer is fully written by one launch before a later launch reads it.
@@ -23,9 +28,9 @@
 // streams, two host threads, or a second call enqueued on another stream before the
 // first finishes) race on it.  Serialise them on one stream, or use
 // qg_layer_slice_forward with a workspace per concurrent caller.
-#include <atomic>
 #include <mutex>
 
+#include "qg_ctx_cache.h"
 #include "qg_host.h"
 
 namespace {
@@ -34,28 +39,68 @@ constexpr int kMaxDevices = 64;
 
 static __device__ __align__(256) uint8_t g_slice_scratch[QG_SLICE_STATIC_SCRATCH_BYTES];
 
-std::atomic<void*> g_scratch_ptr[kMaxDevices];
-std::mutex g_setup_mutex;
+// Driver-API calls resolved once through cudaGetDriverEntryPoint (signatures of
+// cuCtxGetCurrent and cuCtxGetId; CUcontext is an opaque pointer).
+using CtxGetCurrentFn = int (*)(void** ctx);
+using CtxGetIdFn = int (*)(void* ctx, unsigned long long* id);
 
-// Device address of g_slice_scratch on the current device (looked up once per device).
-cudaError_t scratch_for_current_device(void** ptr) {
+std::mutex g_setup_mutex;
+qg::CtxAddressCache<kMaxDevices> g_scratch;
+CtxGetCurrentFn g_ctx_get_current = nullptr;
+CtxGetIdFn g_ctx_get_id = nullptr;
+
+cudaError_t resolve_driver_calls() {
+  if (g_ctx_get_current != nullptr && g_ctx_get_id != nullptr) return cudaSuccess;
+  void* f0 = nullptr;
+  void* f1 = nullptr;
+  cudaDriverEntryPointQueryResult q0 = cudaDriverEntryPointSymbolNotFound, q1 = q0;
+  cudaError_t e = cudaGetDriverEntryPoint("cuCtxGetCurrent", &f0, cudaEnableDefault, &q0);
+  if (e != cudaSuccess) return e;
+  e = cudaGetDriverEntryPoint("cuCtxGetId", &f1, cudaEnableDefault, &q1);
+  if (e != cudaSuccess) return e;
+  if (q0 != cudaDriverEntryPointSuccess || q1 != cudaDriverEntryPointSuccess || f0 == nullptr ||
+      f1 == nullptr) {
+    return cudaErrorNotSupported;
+  }
+  g_ctx_get_current = reinterpret_cast<CtxGetCurrentFn>(f0);
+  g_ctx_get_id = reinterpret_cast<CtxGetIdFn>(f1);
+  return cudaSuccess;
+}
+
+// Device address of g_slice_scratch in the current context (looked up once per context).
+cudaError_t scratch_for_current_context(void** ptr) {
   int dev = -1;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
-  void* p = g_scratch_ptr[dev].load(std::memory_order_acquire);
-  if (p == nullptr) {
-    std::lock_guard<std::mutex> lock(g_setup_mutex);
-    p = g_scratch_ptr[dev].load(std::memory_order_relaxed);
-    if (p == nullptr) {
-      e = cudaGetSymbolAddress(&p, g_slice_scratch);
-      if (e != cudaSuccess) return e;
-      if (p == nullptr || (reinterpret_cast<uintptr_t>(p) & 255u) != 0u) return cudaErrorInvalidSymbol;
-      g_scratch_ptr[dev].store(p, std::memory_order_release);
+  std::lock_guard<std::mutex> lock(g_setup_mutex);
+  e = resolve_driver_calls();
+  if (e != cudaSuccess) return e;
+  void* ctx = nullptr;
+  if (g_ctx_get_current(&ctx) != 0) return cudaErrorDeviceUninitialized;
+  unsigned long long id = 0;
+  if (ctx != nullptr && g_ctx_get_id(ctx, &id) != 0) return cudaErrorDeviceUninitialized;
+  auto lookup = [](void** p) -> int {
+    const cudaError_t le = cudaGetSymbolAddress(p, g_slice_scratch);
+    if (le != cudaSuccess) return static_cast<int>(le);
+    if (*p == nullptr || (reinterpret_cast<uintptr_t>(*p) & 255u) != 0u) {
+      return static_cast<int>(cudaErrorInvalidSymbol);
+    }
+    return 0;
+  };
+  if (ctx == nullptr) {
+    // No context yet: the lookup makes the device's primary context current; cache the
+    // address under that context's id.
+    void* p = nullptr;
+    const int rc = lookup(&p);
+    if (rc != 0) return static_cast<cudaError_t>(rc);
+    if (g_ctx_get_current(&ctx) != 0 || ctx == nullptr || g_ctx_get_id(ctx, &id) != 0) {
+      return cudaErrorDeviceUninitialized;
     }
   }
-  *ptr = p;
-  return cudaSuccess;
+  const int rc = g_scratch.get(dev, id, lookup, ptr);
+  if (rc < 0) return cudaErrorInvalidDevice;
+  return static_cast<cudaError_t>(rc);
 }
 
 }  // namespace
@@ -69,7 +114,7 @@ extern "C" cudaError_t qg_layer_slice_forward_static(const qg_layer_slice* s, co
   if (need > QG_SLICE_STATIC_SCRATCH_BYTES) return cudaErrorInvalidValue;
   if (x == nullptr || out == nullptr) return cudaErrorInvalidValue;
   void* scratch = nullptr;
-  e = scratch_for_current_device(&scratch);
+  e = scratch_for_current_context(&scratch);
   if (e != cudaSuccess) return e;
   return qg_layer_slice_forward(s, x, out, scratch, stream);
 }

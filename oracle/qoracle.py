@@ -24,7 +24,9 @@ import numpy as np
 HERE = Path(__file__).resolve().parent
 PORT_LIB = HERE / "_build" / "libqoracle.so"
 REF_LIB = HERE / "_ref" / "libref_oracle.so"
-REFERENCE_ROOT = Path(os.environ.get("QG_REFERENCE_ROOT", "/root/reference"))
+# The reference tree: QG_REFERENCE_ROOT, else a checkout named "reference" beside this
+# repository (absent on machines that only run the prebuilt files).
+REFERENCE_ROOT = Path(os.environ.get("QG_REFERENCE_ROOT", str(HERE.parent.parent / "reference")))
 
 
 def _p(a: np.ndarray | None):

@@ -16,7 +16,7 @@ import pytest
 from conftest import FORMAT_TAGS, GOLDEN, REPO, load_golden
 from qgemv_b200 import packs
 
-REF_ROOT = Path("/root/reference")
+from qoracle import REFERENCE_ROOT as REF_ROOT  # noqa: E402
 
 
 def same_bits(a: np.ndarray, b: np.ndarray) -> bool:

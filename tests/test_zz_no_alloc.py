@@ -10,7 +10,7 @@ import pytest
 import torch
 
 import qgemv_b200
-from qgemv_b200 import packs
+from qgemv_b200 import ops, packs
 from qgemv_b200._lib import check
 from qgemv_b200.slice import LayerSlice, LayerSliceC
 
@@ -65,3 +65,29 @@ def test_static_matches_workspace_forward_twice(cuda, dims):
         # same kernels on the same inputs: expected identical, checked within 1e-6 relative
         np.testing.assert_allclose(g, w, rtol=1e-6, atol=1e-6 * float(np.abs(w).max()),
                                    err_msg=f"call {call}")
+
+
+@pytest.mark.gpu
+def test_static_back_to_back_on_one_stream(cuda):
+    """Three static calls enqueued on one stream with no host synchronisation between them
+    (each kernel's prologue may overlap the previous kernel through programmatic dependent
+    launch while they share the one scratch array); every output must equal its
+    workspace-path result and the library's error word must stay clear."""
+    dims = dict(hidden=4096, q_rows=4096, kv_rows=1024, ffn=14336)
+    sl = LayerSlice(**dims, seed=23)
+    stream = torch.cuda.current_stream()
+    xs = [torch.from_numpy(packs.synthetic_activation(dims["hidden"], 400 + i)).to(cuda) for i in range(3)]
+    wants = [sl.forward(x) for x in xs]
+    torch.cuda.synchronize()
+    assert ops.get_error() == 0  # read and clear before the static calls
+    outs = [torch.full_like(x, float("nan")) for x in xs]
+    for x, o in zip(xs, outs):
+        check("qg_layer_slice_forward_static", ctypes.byref(sl.c), x.data_ptr(), o.data_ptr(),
+              stream.cuda_stream)
+    torch.cuda.synchronize()
+    for i, (w, o) in enumerate(zip(wants, outs)):
+        w, g = w.cpu().numpy(), o.cpu().numpy()
+        assert np.isfinite(g).all(), f"call {i}: output not fully written"
+        np.testing.assert_allclose(g, w, rtol=1e-6, atol=1e-6 * float(np.abs(w).max()),
+                                   err_msg=f"call {i}")
+    assert ops.get_error() == 0
