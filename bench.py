@@ -403,28 +403,33 @@ def measure_batched(device, args, peak: float, only: tuple | None = None) -> dic
 def measure_decode(device, args, world: int, rank: int, layers: int | None = None) -> dict:
     """the 80-layer 70B-class mixed-quant decode step (IQ3_S
     attention, IQ2_S gate/up, Q5_K down, Q4_K vocab head, fp16 KV cache at context
-    4096), tensor-parallel over the job's N GPUs, one graph per token.  With N > 1 the
-    step is timed twice on the same weights: the per-layer all-reduces fused into the
-    GEMVs over NVLink peer memory (the reported numbers) and as ncclAllReduce calls
-    between the kernels (`nccl`, the baseline)."""
+    4096), tensor-parallel over the job's N GPUs, one graph per token.  Every rank cuts
+    its shards from the same seeded global weights.  With N > 1 the step is timed twice:
+    exchanges fused into the GEMVs over NVLink peer memory (the reported numbers) and the
+    same exchange words moved by ncclAllGather between the kernels (`nccl`, the baseline);
+    then rank 0 runs the same step unsharded (TP 1, the whole model on one GPU) and
+    reports whether the token and the final hidden state are bit-identical."""
     import torch
     import torch.distributed as dist
 
-    from qgemv_b200 import decoder
+    from qgemv_b200 import decoder, ops
     from qgemv_b200.slice import StepGraph
 
     spec = decoder.ModelSpec() if layers is None else decoder.ModelSpec(layers=layers)
-    w = decoder.synthetic_rank_weights(spec, rank, world, device, seed=1)
-    x = torch.randn(spec.hidden, device=device)
+    w = decoder.synthetic_rank_weights(spec, rank, world, device, seed=1,
+                                       keep_full=(world > 1 and rank == 0))
+    gen = torch.Generator(device=device)
+    gen.manual_seed(4242)
+    x = torch.randn(spec.hidden, device=device, generator=gen)  # same on every rank
     pos = spec.ctx_max - 1
 
-    def timed(collective: int) -> tuple[float, int]:
+    def timed(weights, tp: int, tp_rank: int, collective: int, group: bool) -> dict:
         nid = None
-        if world > 1:
+        if tp > 1:
             obj = [decoder.nccl_unique_id() if rank == 0 else None]
             dist.broadcast_object_list(obj, src=0)
             nid = obj[0]
-        dec = decoder.Decoder(spec, w, rank=rank, tp=world, nccl_id=nid, device=device,
+        dec = decoder.Decoder(spec, weights, rank=tp_rank, tp=tp, nccl_id=nid, device=device,
                               collective=collective)
         stream = torch.cuda.Stream(device)
         stream.wait_stream(torch.cuda.current_stream(device))
@@ -438,7 +443,7 @@ def measure_decode(device, args, world: int, rank: int, layers: int | None = Non
             if i % 4 == 3:
                 stream.synchronize()
         stream.synchronize()
-        if world > 1:
+        if group:
             dist.barrier()
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
@@ -448,29 +453,50 @@ def measure_decode(device, args, world: int, rank: int, layers: int | None = Non
         e1.record(stream)
         stream.synchronize()
         ms = e0.elapsed_time(e1) / args.steps
-        if world > 1:
+        # a bounded exchange wait that ran out fails the measurement (the error word is
+        # sticky over the replays)
+        err = ops.get_error()
+        if err:
+            raise RuntimeError(f"decode step (tp {tp}) set error word {err:#x}")
+        if group:
             t = torch.tensor([ms], dtype=torch.float64, device=device)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             ms = float(t.item())
-        token = int(dec.token.item())
+        out = {"ms_per_token": ms, "tok_per_s": 1000.0 / ms, "token": int(dec.token.item()),
+               "hidden": dec.hidden().clone()}
         g.close()
         dec.close()
-        return ms, token
+        return out
 
-    ms, token = timed(decoder.COLLECTIVE_NVLINK)
-    nccl = None
+    fused = timed(w, world, rank, decoder.COLLECTIVE_NVLINK, world > 1)
+    res = {"workload": f"BASELINE config 5: {spec.layers}-layer 70B-class decode step, ctx 4096, batch 1",
+           "tp": world}
+    moved = spec.weight_bytes() + spec.kv_bytes_read(spec.ctx_max)
+    res.update({"ms_per_token": fused["ms_per_token"], "tok_per_s": fused["tok_per_s"],
+                "token": fused["token"], "GBps_aggregate": moved / (fused["ms_per_token"] * 1e-3) / 1e9,
+                "weight_bytes": spec.weight_bytes(), "kv_bytes": spec.kv_bytes_read(spec.ctx_max),
+                "launches_per_token": spec.layers * 10 + 4})
     if world > 1:
-        ms_n, token_n = timed(decoder.COLLECTIVE_NCCL)
-        nccl = {"ms_per_token": ms_n, "tok_per_s": 1000.0 / ms_n, "token": token_n}
+        nccl = timed(w, world, rank, decoder.COLLECTIVE_NCCL, True)
+        dist.barrier()
+        if rank == 0:
+            # TP 1 on rank 0: the whole model, the same x and position
+            tp1 = timed(w["full"], 1, 0, decoder.COLLECTIVE_NVLINK, False)
+            same = lambda a, b: bool(torch.equal(a.view(torch.int32), b.view(torch.int32)))  # noqa: E731
+            res["collective"] = "fused NVLink exchange in the Wo/Wd GEMVs (pairwise rank tree)"
+            res["nccl"] = {"ms_per_token": nccl["ms_per_token"], "tok_per_s": nccl["tok_per_s"],
+                           "token": nccl["token"], "matches_tp1": nccl["token"] == tp1["token"] and
+                           same(nccl["hidden"], tp1["hidden"])}
+            res["tp1_on_rank0"] = {"ms_per_token": tp1["ms_per_token"], "tok_per_s": tp1["tok_per_s"],
+                                   "token": tp1["token"]}
+            res["token_tp1"] = tp1["token"]
+            res["hidden_bits_equal_tp1"] = same(fused["hidden"], tp1["hidden"])
+            res["matches_tp1"] = fused["token"] == tp1["token"] and res["hidden_bits_equal_tp1"]
+            res["speedup_vs_tp1"] = tp1["ms_per_token"] / fused["ms_per_token"]
+        dist.barrier()
     del w
     torch.cuda.empty_cache()
-    moved = spec.weight_bytes() + spec.kv_bytes_read(spec.ctx_max)
-    return {"workload": f"BASELINE config 5: {spec.layers}-layer 70B-class decode step, ctx 4096, batch 1",
-            "tp": world, "ms_per_token": ms, "tok_per_s": 1000.0 / ms,
-            "collective": "fused NVLink exchange in the Wo/Wd GEMVs" if world > 1 else None,
-            "weight_bytes": spec.weight_bytes(), "kv_bytes": spec.kv_bytes_read(spec.ctx_max),
-            "GBps_aggregate": moved / (ms * 1e-3) / 1e9, "token": token,
-            "launches_per_token": spec.layers * 10 + 4, "nccl": nccl}
+    return res
 
 
 def run_ours(args) -> int:
@@ -720,8 +746,8 @@ def run_ours(args) -> int:
             "per_matvec": per,
             "reference_gpu": ref_gpu,
             "slice": slice_stats,
-            "decode": decode_stats,
             "batched": batched_stats,
+            "decode": decode_stats,  # last: the driver keeps the end of the line
         }
         print(json.dumps(line))
     if world > 1:

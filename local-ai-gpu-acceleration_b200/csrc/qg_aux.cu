@@ -242,99 +242,139 @@ cudaError_t launch_act_prepare(const float* x, uint32_t cols, void* act, cudaStr
 }
 
 
-// RMSNorm + int8 planes of a vector that is either read directly (nsrc = 0: x_in) or
-// gathered from a tensor-parallel exchange, one thread-block cluster of up to 8 CTAs,
-// CTA c owning elements [c n/C, (c+1) n/C).  Every word of every rank's
-// slot carries the epoch it was written for: a thread issues all ranks' loads of an
-// element at once, re-reads (bounded) any word that is not current yet, and sums the
-// ranks in rank order (every rank computes the same bits).  The sum of squares of the
-// RMSNorm is combined across the cluster through distributed shared memory, in CTA
-// order; no CTA polls global memory for another.
+// Canonical sum of squares of an RMSNorm input (every kernel that normalises a hidden
+// vector uses it, so that a vector with the same bits gives the same norm whichever
+// kernel -- plain or gathering -- computes it): 256 threads, thread t accumulating the
+// float4 elements j = t, t + 256, ... with one fmaf per value in element order, then a
+// butterfly over each warp (lane bits 16, 8, 4, 2, 1) and the eight warp sums left to
+// right.  `load4(j)` returns elements 4j .. 4j + 3.
+constexpr uint32_t kSumThreads = 256;
+
+template <typename Load4>
+__device__ __forceinline__ float canon_sumsq(uint32_t n4, float* ws, Load4 load4) {
+  const uint32_t t = threadIdx.x;
+  if (t < kSumThreads) {
+    float sq = 0.f;
+#pragma unroll 4
+    for (uint32_t j = t; j < n4; j += kSumThreads) {
+      const float4 v = load4(j);
+      sq = fmaf(v.x, v.x, sq);
+      sq = fmaf(v.y, v.y, sq);
+      sq = fmaf(v.z, v.z, sq);
+      sq = fmaf(v.w, v.w, sq);
+    }
+    for (int off = 16; off > 0; off >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, off);
+    if ((t & 31u) == 0u) ws[t >> 5] = sq;
+  }
+  __syncthreads();
+  float total = 0.f;
+#pragma unroll
+  for (uint32_t k = 0; k < kSumThreads / 32u; ++k) total += ws[k];
+  return total;
+}
+
+// RMSNorm + int8 planes of a vector gathered from a tensor-parallel exchange, one
+// thread-block cluster of up to 8 CTAs, CTA c owning elements [c n/C, (c+1) n/C).  Every
+// word of every rank's slot carries the epoch it was written for: a thread issues all
+// ranks' loads of an element at once and re-reads (bounded) any word that is not current
+// yet.  The ranks' values are added in a pairwise tree (ranks 0+1, 2+3, ..., then the
+// pairs), the same tree the row-parallel GEMV uses for the segments of a single-GPU row,
+// and then added to the residual: x_out = residual + tree, the single-GPU result bit for
+// bit.  A word that never becomes current makes its element NaN (and sets
+// QG_ERR_WAIT_TIMEOUT), so a failed exchange cannot pass for a result.  Each CTA keeps its
+// elements in shared memory; the canonical sum of squares then reads the whole vector
+// from the cluster's distributed shared memory, so every CTA (and the plain
+// norm_prepare_kernel on the same vector) holds the same bits.
 constexpr uint32_t kMaxWordPolls = 1u << 20;  // per word, with 32 ns sleeps after the first few
 
 __global__ void __launch_bounds__(1024) gather_norm_prepare_kernel(
-    const uint64_t* buf, uint32_t* epoch, uint32_t nsrc, uint32_t stride, const float* x_in,
+    const uint64_t* buf, uint32_t* epoch, uint32_t nsrc, uint32_t stride, const float* residual,
     const float* __restrict__ w, uint32_t n, float eps, float* x_out, float* h, ActChunk* act) {
   namespace cg = cooperative_groups;
   cg::cluster_group cluster = cg::this_cluster();
+  extern __shared__ __align__(16) float xs[];  // this CTA's elements
   __shared__ float ws[32];
-  __shared__ float part;
   __shared__ uint32_t gave_up;
   pdl_wait();
   pdl_trigger();
   const uint32_t cta = cluster.block_rank(), ncta = cluster.num_blocks();
-  const uint32_t E = nsrc != 0u ? *epoch + 1u : 0u;
-  const uint64_t* base = nsrc != 0u ? buf + (E & 1u) * static_cast<size_t>(stride) : nullptr;
+  const uint32_t E = *epoch + 1u;
+  const uint64_t* base = buf + (E & 1u) * static_cast<size_t>(stride);
   if (threadIdx.x == 0u) gave_up = 0u;
   cluster.sync();  // every CTA has read the epoch before it advances
-  if (nsrc != 0u && cta == 0u && threadIdx.x == 0u) *epoch = E;
+  if (cta == 0u && threadIdx.x == 0u) *epoch = E;
   const uint32_t per = n / ncta, lo = cta * per;
-  float sq = 0.f;
   for (uint32_t i = lo + threadIdx.x; i < lo + per; i += blockDim.x) {
     uint64_t word[kMaxExchangeRanks];
 #pragma unroll
     for (uint32_t s = 0; s < kMaxExchangeRanks; ++s) {
       if (s < nsrc) word[s] = ld_relaxed_sys_u64(base + static_cast<size_t>(s) * n + i);
     }
-    float v = nsrc == 0u ? x_in[i] : 0.f;
+    float r[kMaxExchangeRanks];
 #pragma unroll
     for (uint32_t s = 0; s < kMaxExchangeRanks; ++s) {
-      if (s >= nsrc) break;
+      r[s] = 0.f;
+      if (s >= nsrc) continue;
+      bool ok = true;
       for (uint32_t it = 0; static_cast<uint32_t>(word[s] >> 32) != E; ++it) {
         if (it == kMaxWordPolls || *reinterpret_cast<volatile uint32_t*>(&gave_up) != 0u) {
           if (atomicExch(&gave_up, 1u) == 0u) atomicOr(&g_error_word, QG_ERR_WAIT_TIMEOUT);
+          ok = false;
           break;
         }
         if (it > 8u) __nanosleep(32);
         word[s] = ld_relaxed_sys_u64(base + static_cast<size_t>(s) * n + i);
       }
-      v += __uint_as_float(static_cast<uint32_t>(word[s]));
+      r[s] = ok ? __uint_as_float(static_cast<uint32_t>(word[s])) : __uint_as_float(0x7fc00000u);
     }
-    if (nsrc != 0u) x_out[i] = v;
-    sq += v * v;
-  }
-  for (int off = 16; off > 0; off >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, off);
-  if ((threadIdx.x & 31u) == 0u) ws[threadIdx.x >> 5] = sq;
-  __syncthreads();
-  if (threadIdx.x < 32u) {
-    sq = threadIdx.x < (blockDim.x >> 5) ? ws[threadIdx.x] : 0.f;
-    for (int off = 16; off > 0; off >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, off);
-    if (threadIdx.x == 0u) part = sq;
-  }
-  cluster.sync();  // every CTA's partial sum of squares is in its shared memory
-  float pc[8];
 #pragma unroll
-  for (uint32_t c = 0; c < 8u; ++c) pc[c] = c < ncta ? *cluster.map_shared_rank(&part, c) : 0.f;
-  float total = 0.f;
+    for (uint32_t step = 1; step < kMaxExchangeRanks; step <<= 1) {
 #pragma unroll
-  for (uint32_t c = 0; c < 8u; ++c) total += pc[c];  // CTA order (the unused slots add 0)
+      for (uint32_t s = 0; s + step < kMaxExchangeRanks; s += 2u * step) {
+        if (s + step < nsrc) r[s] += r[s + step];
+      }
+    }
+    const float v = residual != nullptr ? residual[i] + r[0] : r[0];
+    x_out[i] = v;
+    xs[i - lo] = v;
+  }
+  cluster.sync();  // every CTA's elements are in its shared memory
+  const float total = canon_sumsq(n / 4u, ws, [&](uint32_t j) {
+    const uint32_t owner = (4u * j) / per;
+    const float* src = cluster.map_shared_rank(xs, owner);
+    return *reinterpret_cast<const float4*>(src + (4u * j - owner * per));
+  });
   const float inv = 1.0f / sqrtf(total / static_cast<float>(n) + eps);
   const uint32_t lane = threadIdx.x & 31u;
-  const float* xv = nsrc != 0u ? x_out : x_in;
   for (uint32_t c = lo / 64u + (threadIdx.x >> 5); c < (lo + per) / 64u; c += blockDim.x >> 5) {
     const uint32_t i = 64u * c + 2u * lane;
-    const float v0 = xv[i] * inv * w[i], v1 = xv[i + 1u] * inv * w[i + 1u];
+    const float v0 = xs[i - lo] * inv * w[i], v1 = xs[i + 1u - lo] * inv * w[i + 1u];
     if (h != nullptr) {
       h[i] = v0;
       h[i + 1u] = v1;
     }
     warp_prepare_chunk(v0, v1, act + c);
   }
-  cluster.sync();  // no CTA leaves while another may still read its partial
+  cluster.sync();  // no CTA leaves while another may still read its elements
 }
 
-namespace {
-cudaError_t launch_cluster_norm(const uint64_t* buf, uint32_t* epoch, uint32_t nsrc, uint32_t stride,
-                                const float* x_in, const float* w, uint32_t n, float eps,
-                                float* x_out, float* h, void* act, cudaStream_t stream) {
-  if (nsrc > kMaxExchangeRanks || n == 0u || n % 64u != 0u) return cudaErrorInvalidValue;
+cudaError_t launch_gather_norm_prepare(const uint64_t* buf, uint32_t* epoch, uint32_t nsrc,
+                                       uint32_t stride, const float* residual, const float* w,
+                                       uint32_t n, float eps, float* x_out, float* h, void* act,
+                                       cudaStream_t stream) {
+  if (nsrc == 0u || nsrc > kMaxExchangeRanks || buf == nullptr || epoch == nullptr ||
+      x_out == nullptr || n == 0u || n % 64u != 0u) {
+    return cudaErrorInvalidValue;
+  }
   // CTAs: up to 8, each owning a whole number of 64-column chunks and >= 1024 elements
   uint32_t ncta = 8u;
   while (ncta > 1u && (n % (64u * ncta) != 0u || n / ncta < 1024u)) ncta >>= 1;
+  const uint32_t smem = (n / ncta) * 4u;
+  if (smem > 48u * 1024u) return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(ncta);
   cfg.blockDim = dim3(1024);
-  cfg.dynamicSmemBytes = 0;
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -345,24 +385,16 @@ cudaError_t launch_cluster_norm(const uint64_t* buf, uint32_t* epoch, uint32_t n
   attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  return cudaLaunchKernelEx(&cfg, gather_norm_prepare_kernel, buf, epoch, nsrc, stride, x_in, w, n,
-                            eps, x_out, h, static_cast<ActChunk*>(act));
-}
-}  // namespace
-
-cudaError_t launch_gather_norm_prepare(const uint64_t* buf, uint32_t* epoch, uint32_t nsrc,
-                                       uint32_t stride, const float* w, uint32_t n, float eps,
-                                       float* x_out, float* h, void* act, cudaStream_t stream) {
-  if (nsrc == 0u || buf == nullptr || epoch == nullptr || x_out == nullptr) return cudaErrorInvalidValue;
-  return launch_cluster_norm(buf, epoch, nsrc, stride, nullptr, w, n, eps, x_out, h, act, stream);
+  return cudaLaunchKernelEx(&cfg, gather_norm_prepare_kernel, buf, epoch, nsrc, stride, residual, w,
+                            n, eps, x_out, h, static_cast<ActChunk*>(act));
 }
 
 // h = x / sqrt(mean(x^2) + eps) * w and h's int8 planes (the layer slice's and the
-// decoder's RMSNorm when there is nothing to gather).  No cluster: every CTA sums the
-// squares of the whole vector itself (it was just written, so it is read from L2), with
-// the same loads and the same reduction order in every CTA, so all CTAs hold the same
-// bits; then each normalises and prepares its own 64-column chunks, one warp per chunk.
-constexpr uint32_t kNormThreads = 256;
+// decoder's RMSNorm when there is nothing to gather).  No cluster: every CTA computes the
+// canonical sum of squares of the whole vector itself (it was just written, so it is read
+// from L2), so all CTAs hold the same bits; then each normalises and prepares its own
+// 64-column chunks, one warp per chunk.
+constexpr uint32_t kNormThreads = kSumThreads;
 
 __global__ void __launch_bounds__(kNormThreads) norm_prepare_kernel(const float* __restrict__ x,
                                                                     const float* __restrict__ w,
@@ -371,28 +403,17 @@ __global__ void __launch_bounds__(kNormThreads) norm_prepare_kernel(const float*
   __shared__ float ws[kNormThreads / 32u];
   pdl_wait();
   pdl_trigger();
-  float sq = 0.f;
+  float total;
   if ((reinterpret_cast<uintptr_t>(x) & 15u) == 0u) {
     const float4* x4 = reinterpret_cast<const float4*>(x);
-#pragma unroll 4
-    for (uint32_t i = threadIdx.x; i < n / 4u; i += kNormThreads) {
-      const float4 v = x4[i];
-      sq = fmaf(v.x, v.x, sq);
-      sq = fmaf(v.y, v.y, sq);
-      sq = fmaf(v.z, v.z, sq);
-      sq = fmaf(v.w, v.w, sq);
-    }
+    total = canon_sumsq(n / 4u, ws, [&](uint32_t j) { return x4[j]; });
   } else {
-    for (uint32_t i = threadIdx.x; i < n; i += kNormThreads) sq = fmaf(x[i], x[i], sq);
+    total = canon_sumsq(n / 4u, ws, [&](uint32_t j) {
+      return make_float4(x[4u * j], x[4u * j + 1u], x[4u * j + 2u], x[4u * j + 3u]);
+    });
   }
-  for (int off = 16; off > 0; off >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, off);
-  const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
-  if (lane == 0u) ws[warp] = sq;
-  __syncthreads();
-  float total = 0.f;
-#pragma unroll
-  for (uint32_t k = 0; k < kNormThreads / 32u; ++k) total += ws[k];
   const float inv = 1.0f / sqrtf(total / static_cast<float>(n) + eps);
+  const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
   const uint32_t c = blockIdx.x * (kNormThreads / 32u) + warp;
   if (c < n / 64u) {
     const uint32_t i = 64u * c + 2u * lane;

@@ -7,20 +7,28 @@
 //   column shards Wo (its q heads' columns), Wd (its ffn/N columns);
 //   its kv heads' fp16 KV cache.
 // Per layer:  h = rmsnorm(x)*w_attn -> q,k,v (one GEMV launch) -> RoPE + cache append
-//   -> GQA decode attention -> Wo (partial; rank 0 adds the residual x) -> all-reduce
-//   -> rmsnorm*w_ffn -> gate,up (one launch) -> silu(g)*u -> Wd (partial; rank 0 adds
-//   the residual) -> all-reduce.  After the last layer: final rmsnorm -> vocab-shard GEMV
-//   -> shard argmax -> all-gather of (value, index) -> token.
-// The two all-reduces per layer are fused into the kernels around them, over NVLink
-// peer memory: the Wo / Wd GEMV stores every output row straight into each rank's
-// exchange buffer (this rank's slot) as 64-bit words that carry the exchange's epoch;
-// the next kernel (RMSNorm + int8 planes, which reads the whole vector anyway) reads
-// every rank's slot until each word is current, sums the ranks in rank order and
-// normalises.  No extra launch, fence, flag or collective library call on the hot path;
-// buffers are double-buffered by epoch parity, so a rank can run at most one exchange
-// ahead of the slowest one.  The
+//   -> GQA decode attention -> Wo (partial) -> exchange -> x1 = x + sum of partials
+//   -> rmsnorm*w_ffn -> gate,up (one launch) -> silu(g)*u -> Wd (partial) -> exchange
+//   -> x2 = x1 + sum.  After the last layer: final rmsnorm -> vocab-shard GEMV -> shard
+//   argmax -> all-gather of (value, index) -> token.
+// Every tensor-parallel degree computes the single-GPU step bit for bit: the column-
+// parallel rows (Q/K/V, gate/up, head) are whole rows on one rank; the row-parallel
+// Wo / Wd sums follow one canonical order (8 column segments = the shards at TP 8,
+// each summed in a fixed order, then a pairwise tree; a rank's GEMV computes its
+// subtree, the exchange gather adds the ranks in the same tree and then the residual);
+// the RMSNorm sum of squares has one fixed order in both the plain and the gathering
+// kernel.
+// The two exchanges per layer are fused into the kernels around them, over NVLink peer
+// memory: the Wo / Wd GEMV stores every output row straight into each rank's exchange
+// buffer (this rank's slot) as 64-bit words that carry the exchange's epoch; the next
+// kernel (RMSNorm + int8 planes, which reads the whole vector anyway) reads every rank's
+// slot until each word is current, sums the ranks and normalises.  No extra launch,
+// fence, flag or collective library call on the hot path; buffers are double-buffered
+// by epoch parity, so a rank can run at most one exchange ahead of the slowest one.  The
 // exchange buffers are allocated by qg_decoder_create and shared through CUDA IPC
-// (handles gathered with NCCL once).  NCCL carries only the token's all-gather.
+// (handles gathered with NCCL once).  NCCL carries only the token's all-gather.  The
+// baseline mode (collective = 1) moves the same words with ncclAllGather into a local
+// buffer instead of peer stores, so it gives the same bits as well.
 // Every launch goes on the caller's stream, so one decode step can be captured into one
 // CUDA graph (qg_graph_begin / qg_graph_end).
 #include <nccl.h>
@@ -68,6 +76,19 @@ Shape shard_shape(const qg_decoder_dims* d) {
   return s;
 }
 
+// Canonical segments of a row-parallel matrix with `full_cols` columns (all ranks): the
+// largest P in {8, 4, 2, 1} that cuts the row into whole 256-column blocks; a rank of tp
+// holds P / tp of them (tensor-parallel shards are whole blocks, so P >= tp).
+qg::GemvCanon canon_of(uint32_t full_cols, uint32_t tp) {
+  uint32_t P = 8u;
+  while (P > 1u && full_cols % (256u * P) != 0u) P >>= 1;
+  qg::GemvCanon c{};
+  if (P % tp != 0u) return c;  // no canonical split for this degree (nseg = 0)
+  c.nseg = P / tp;
+  c.seg_chunks = full_cols / (64u * P);
+  return c;
+}
+
 bool dims_ok(const qg_decoder_dims* d) {
   if (d == nullptr || d->tp_size == 0u || d->tp_rank >= d->tp_size || d->layers == 0u) return false;
   if (d->head_dim != 128u || d->n_kv_heads == 0u || d->n_q_heads % d->n_kv_heads != 0u) return false;
@@ -75,12 +96,14 @@ bool dims_ok(const qg_decoder_dims* d) {
   const uint32_t group = d->n_q_heads / d->n_kv_heads;
   if (group > 16u || (group & (group - 1u)) != 0u) return false;  // attention: G in {1,2,4,8,16}
   if (d->ffn % d->tp_size != 0u || d->vocab < d->tp_size || d->ctx_max == 0u) return false;
-  if (d->collective > 1u || (d->tp_size > 1u && d->collective == 0u && d->tp_size > qg::kMaxExchangeRanks)) {
-    return false;
-  }
+  if (d->collective > 1u || d->tp_size > qg::kMaxExchangeRanks) return false;
   const Shape s = shard_shape(d);
   auto width_ok = [](uint32_t n) { return n != 0u && n % 256u == 0u && n / 64u <= 512u; };
   if (!width_ok(d->hidden) || !width_ok(s.q_local) || !width_ok(s.ffn_local)) return false;
+  if (canon_of(d->n_q_heads * d->head_dim, d->tp_size).nseg == 0u ||
+      canon_of(d->ffn, d->tp_size).nseg == 0u) {
+    return false;
+  }
   for (int f : {d->attn_fmt, d->ffn_fmt, d->down_fmt, d->head_fmt}) {
     if (f < 0 || f >= QG_FMT_COUNT) return false;
   }
@@ -149,6 +172,8 @@ struct qg_decoder_s {
   uint32_t last_output = 0;  // workspace offset of the last step's final hidden state
   uint8_t* ex_local = nullptr;                   // this rank's exchange region
   uint8_t* ex_peer[qg::kMaxExchangeRanks] = {};  // every rank's region (self included)
+  qg::GemvCanon canon_o{}, canon_d{};            // canonical segments of Wo / Wd on this rank
+  bool broken = false;                           // a step failed after enqueueing work
 };
 
 namespace {
@@ -163,6 +188,11 @@ cudaError_t exchange_setup(qg_decoder_s* dec) {
   if (e != cudaSuccess) return e;
   e = cudaMemset(dec->ex_local, 0, bytes);
   if (e != cudaSuccess) return e;
+  if (dec->dims.collective != 0u) {  // NCCL moves the words: the local region only
+    e = cudaDeviceSynchronize();
+    dec->ex_peer[r] = dec->ex_local;
+    return e;
+  }
   cudaIpcMemHandle_t mine;
   e = cudaIpcGetMemHandle(&mine, dec->ex_local);
   if (e != cudaSuccess) return e;
@@ -205,14 +235,16 @@ void exchange_teardown(qg_decoder_s* dec) {
   dec->ex_local = nullptr;
 }
 
-// The Wo / Wd GEMV side of an exchange.
+// The Wo / Wd GEMV side of an exchange: this rank's slot in every rank's region (fused
+// mode), or in its own region only (NCCL mode: ncclAllGather then copies the slots).
 qg::GemvExchange exchange_out(const qg_decoder_s* dec) {
   qg::GemvExchange ex{};
   const uint32_t n = dec->dims.tp_size, r = dec->dims.tp_rank, hid = dec->dims.hidden;
-  ex.n = n;
+  ex.n = dec->dims.collective == 0u ? n : 1u;
   ex.stride = n * hid;
-  for (uint32_t p = 0; p < n; ++p) {
-    ex.out[p] = reinterpret_cast<uint64_t*>(dec->ex_peer[p] + kExHeader) + static_cast<size_t>(r) * hid;
+  for (uint32_t k = 0; k < ex.n; ++k) {
+    const uint32_t p = dec->dims.collective == 0u ? k : r;
+    ex.out[k] = reinterpret_cast<uint64_t*>(dec->ex_peer[p] + kExHeader) + static_cast<size_t>(r) * hid;
   }
   ex.epoch = reinterpret_cast<const uint32_t*>(dec->ex_local + kExEpoch);
   return ex;
@@ -269,6 +301,8 @@ cudaError_t qg_decoder_create(const qg_decoder_dims* d, const qg_decoder_layer* 
   dec->head = head;
   dec->head_meta = head_meta;
   dec->ws = static_cast<uint8_t*>(workspace);
+  dec->canon_o = canon_of(d->n_q_heads * d->head_dim, d->tp_size);
+  dec->canon_d = canon_of(d->ffn, d->tp_size);
   if (d->tp_size > 1u) {
     ncclUniqueId id;
     std::memcpy(&id, nccl_id, sizeof(id));
@@ -278,7 +312,7 @@ cudaError_t qg_decoder_create(const qg_decoder_dims* d, const qg_decoder_layer* 
       delete dec;
       return cudaErrorUnknown;
     }
-    const cudaError_t e = d->collective == 0u ? exchange_setup(dec) : cudaSuccess;
+    const cudaError_t e = exchange_setup(dec);
     if (e != cudaSuccess) {
       exchange_teardown(dec);
       ncclCommDestroy(dec->comm);
@@ -304,13 +338,13 @@ cudaError_t qg_decoder_step(qg_decoder dec, const float* x, uint32_t pos, uint32
   if (dec == nullptr || x == nullptr || token == nullptr || pos >= dec->dims.ctx_max) {
     return cudaErrorInvalidValue;
   }
+  if (dec->broken) return cudaErrorIllegalState;
   const qg_decoder_dims& d = dec->dims;
   const Shape& s = dec->shape;
   const Layout& L = dec->lay;
   uint8_t* w = dec->ws;
   auto F = [&](size_t off) { return reinterpret_cast<float*>(w + off); };
   const bool tp = d.tp_size > 1u;
-  const bool rank0 = d.tp_rank == 0u;
   float* x1 = F(L.x1);
   float* h = F(L.h);
   float* q = F(L.q);
@@ -322,40 +356,60 @@ cudaError_t qg_decoder_step(qg_decoder dec, const float* x, uint32_t pos, uint32
   float* u = F(L.u);
   float* a = F(L.a);
   cudaError_t e = cudaSuccess;
-#define QG_TRY(expr)            \
-  do {                          \
-    e = (expr);                 \
-    if (e != cudaSuccess) return e; \
+  // Once work of this step is enqueued, a failure leaves the exchange epochs of the
+  // ranks out of step: the decoder refuses further steps.
+  bool enqueued = false;
+#define QG_TRY(expr)                         \
+  do {                                       \
+    e = (expr);                              \
+    if (e != cudaSuccess) {                  \
+      if (enqueued) dec->broken = true;      \
+      return e;                              \
+    }                                        \
+    enqueued = true;                         \
   } while (0)
   const float* cur = x;
   size_t out_off = L.xa;
-  // With tensor parallelism each layer's output stays in the exchange buffers until the
-  // next RMSNorm gathers it (pending); the gather writes the summed vector to its x_out.
+  // With tensor parallelism each row-parallel GEMV's partial stays in the exchange
+  // buffers until the next RMSNorm gathers it (pending); the gather writes
+  // residual + sum of the ranks to its x_out.
   bool pending = false;
-  const bool fused = tp && d.collective == 0u;
-  const qg::GemvExchange ex = fused ? exchange_out(dec) : qg::GemvExchange{};
-  const uint64_t* ex_buf = fused ? reinterpret_cast<const uint64_t*>(dec->ex_local + kExHeader) : nullptr;
-  uint32_t* ex_epoch = fused ? reinterpret_cast<uint32_t*>(dec->ex_local + kExEpoch) : nullptr;
+  const float* pending_residual = nullptr;
+  uint32_t exchanges = 0;  // exchanges of this step so far (the parity of the next one)
+  const qg::GemvExchange ex = tp ? exchange_out(dec) : qg::GemvExchange{};
+  const uint64_t* ex_buf = tp ? reinterpret_cast<const uint64_t*>(dec->ex_local + kExHeader) : nullptr;
+  uint32_t* ex_epoch = tp ? reinterpret_cast<uint32_t*>(dec->ex_local + kExEpoch) : nullptr;
   auto norm = [&](const float* src, float* gathered, const float* weight) -> cudaError_t {
     if (pending) {
       pending = false;
-      return qg::launch_gather_norm_prepare(ex_buf, ex_epoch, d.tp_size, ex.stride, weight, d.hidden,
-                                            d.eps, gathered, h, w + L.act_x, stream);
+      return qg::launch_gather_norm_prepare(ex_buf, ex_epoch, d.tp_size, ex.stride,
+                                            pending_residual, weight, d.hidden, d.eps, gathered, h,
+                                            w + L.act_x, stream);
     }
     return qg::launch_norm_prepare(src, weight, d.hidden, d.eps, h, w + L.act_x, stream);
   };
+  // Row-parallel projection: dst = residual + W in (TP 1), or this rank's partial into
+  // the exchange (the gather adds the ranks and the residual).
   auto project_out = [&](int fmt, const uint8_t* wt, const uint8_t* wm, const float* in,
-                         const void* act, float* dst, const float* residual,
-                         uint32_t cols) -> cudaError_t {
-    if (fused) {
-      pending = true;
-      return qg::launch_gemv_exchange(fmt, wt, wm, in, act, opart, residual, d.hidden, cols, ex,
-                                      stream);
+                         const void* act, float* dst, const float* residual, uint32_t cols,
+                         const qg::GemvCanon& canon) -> cudaError_t {
+    if (!tp) {
+      return qg::launch_gemv_canonical(fmt, wt, wm, in, act, dst, residual, d.hidden, cols, canon,
+                                       stream);
     }
-    const cudaError_t e = qg::launch_gemv(fmt, wt, wm, in, act, tp ? opart : dst, residual, nullptr,
-                                          nullptr, 0u, 0u, 0u, d.hidden, cols, stream);
-    if (e != cudaSuccess || !tp) return e;
-    return nccl_status(ncclAllReduce(opart, dst, d.hidden, ncclFloat, ncclSum, dec->comm, stream));
+    pending = true;
+    pending_residual = residual;
+    // Every step runs an even number of exchanges and the epoch starts at 0, so the
+    // k-th exchange of a step (from 0) has epoch parity (k + 1) & 1.
+    const uint32_t parity = (exchanges + 1u) & 1u;
+    ++exchanges;
+    cudaError_t e2 = qg::launch_gemv_exchange(fmt, wt, wm, in, act, opart, nullptr, d.hidden, cols,
+                                              ex, canon, stream);
+    if (e2 != cudaSuccess || d.collective == 0u) return e2;
+    uint64_t* half = reinterpret_cast<uint64_t*>(dec->ex_local + kExHeader) +
+                     static_cast<size_t>(parity) * ex.stride;
+    return nccl_status(ncclAllGather(half + static_cast<size_t>(d.tp_rank) * d.hidden, half, d.hidden,
+                                     ncclUint64, dec->comm, stream));
   };
   for (uint32_t l = 0; l < d.layers; ++l) {
     const qg_decoder_layer& W = dec->layers[l];
@@ -376,8 +430,8 @@ cudaError_t qg_decoder_step(qg_decoder dec, const float* x, uint32_t pos, uint32
                                   d.ctx_max, pos, d.rope_base, stream));
     QG_TRY(qg::launch_attention(q, W.k_cache, W.v_cache, s.nq_local, s.nkv_local, d.ctx_max,
                                 pos + 1u, F(L.partial), attn, w + L.act_attn, stream));
-    QG_TRY(project_out(d.attn_fmt, W.wo, W.wo_meta, attn, w + L.act_attn, x1, rank0 ? cur : nullptr,
-                       s.q_local));
+    QG_TRY(project_out(d.attn_fmt, W.wo, W.wo_meta, attn, w + L.act_attn, x1, cur, s.q_local,
+                       dec->canon_o));
     // feed-forward block (the exchange of Wo is gathered into x1)
     QG_TRY(norm(x1, x1, W.ffn_norm));
     {
@@ -388,8 +442,8 @@ cudaError_t qg_decoder_step(qg_decoder dec, const float* x, uint32_t pos, uint32
       QG_TRY(qg::launch_gemv_multi(d.ffn_fmt, 2, p, m, y, r, d.hidden, h, w + L.act_x, stream));
     }
     QG_TRY(qg::launch_silu_gate_prepare(g, u, s.ffn_local, a, w + L.act_a, stream));
-    QG_TRY(project_out(d.down_fmt, W.wd, W.wd_meta, a, w + L.act_a, x2, rank0 ? x1 : nullptr,
-                       s.ffn_local));
+    QG_TRY(project_out(d.down_fmt, W.wd, W.wd_meta, a, w + L.act_a, x2, x1, s.ffn_local,
+                       dec->canon_d));
     cur = x2;
     out_off = (out_off == L.xa) ? L.xb : L.xa;
   }

@@ -93,6 +93,8 @@ struct GemvArgs {
   uint32_t nseg;
   uint32_t red;           // tiled kernel: passes reduced 4 or 2 at a time (group 32, Q % red == 0), else 0
   GemvExchange ex;        // tiled kernel: optional tensor-parallel exchange of the rows
+  uint32_t canon_spg;     // canonical row sum: reduction groups per segment (0: plain order)
+  uint32_t canon_nseg;    // canonical row sum: segments per row (1, 2, 4 or 8)
 };
 
 // Segment of tile `tile` and the tile's first row inside that segment.
@@ -331,34 +333,65 @@ __device__ __forceinline__ float group_sum(float v, uint32_t group) {
   return v;
 }
 
-// Sums four per-lane values over the 32 lanes of a warp at once, a transposed
-// butterfly: the first two exchanges trade one value of a pair instead of both
-// (6 shuffles for four sums instead of 20).  Lane l ends with the total of
-// v[2 * bit3(l) + bit4(l)], so lanes 0, 16, 8, 24 hold the sums of v[0..3].
-__device__ __forceinline__ float warp_sum4(const float (&v)[4], uint32_t lane) {
-  const bool b4 = (lane & 16u) != 0u, b3 = (lane & 8u) != 0u;
-  const float w0 = (b4 ? v[1] : v[0]) + __shfl_xor_sync(0xffffffffu, b4 ? v[0] : v[1], 16);
-  const float w1 = (b4 ? v[3] : v[2]) + __shfl_xor_sync(0xffffffffu, b4 ? v[2] : v[3], 16);
-  float u = (b3 ? w1 : w0) + __shfl_xor_sync(0xffffffffu, b3 ? w0 : w1, 8);
-  u += __shfl_xor_sync(0xffffffffu, u, 4);
-  u += __shfl_xor_sync(0xffffffffu, u, 2);
-  u += __shfl_xor_sync(0xffffffffu, u, 1);
+// Sums four per-lane values over each aligned group of G lanes (G = 4, 8, 16 or 32,
+// warp-uniform) at once, a transposed butterfly: the first two exchanges (lane bits G/2
+// and G/4) trade one value of a pair instead of both (for G = 32: 6 shuffles for four
+// sums instead of 20).  Lane l ends with the total of v[2 * bit(G/4) + bit(G/2)], so the
+// lanes whose bits below G/4 are zero hold the group's four sums.  Every sum is the
+// same tree as group_sum's: pairs differing in lane bit G/2 first, then G/4, ..., 1.
+__device__ __forceinline__ float warp_sum4(const float (&v)[4], uint32_t lane, uint32_t G) {
+  const uint32_t h = G >> 1, q = G >> 2;
+  const bool bh = (lane & h) != 0u, bq = (lane & q) != 0u;
+  const float w0 = (bh ? v[1] : v[0]) + __shfl_xor_sync(0xffffffffu, bh ? v[0] : v[1], h);
+  const float w1 = (bh ? v[3] : v[2]) + __shfl_xor_sync(0xffffffffu, bh ? v[2] : v[3], h);
+  float u = (bq ? w1 : w0) + __shfl_xor_sync(0xffffffffu, bq ? w0 : w1, q);
+  for (uint32_t off = G >> 3; off > 0u; off >>= 1) u += __shfl_xor_sync(0xffffffffu, u, off);
   return u;
 }
 
-// The two-value form: lane l ends with the total of v[bit4(l)] (lanes 0 and 16 hold
-// the sums of v[0] and v[1]); 5 shuffles instead of 10.
-__device__ __forceinline__ float warp_sum2(const float (&v)[2], uint32_t lane) {
-  const bool b4 = (lane & 16u) != 0u;
-  float u = (b4 ? v[1] : v[0]) + __shfl_xor_sync(0xffffffffu, b4 ? v[0] : v[1], 16);
-  u += __shfl_xor_sync(0xffffffffu, u, 8);
-  u += __shfl_xor_sync(0xffffffffu, u, 4);
-  u += __shfl_xor_sync(0xffffffffu, u, 2);
-  u += __shfl_xor_sync(0xffffffffu, u, 1);
+// The two-value form: lane l ends with the total of v[bit(G/2)] (the lanes whose bits
+// below G/2 are zero hold the group's two sums).
+__device__ __forceinline__ float warp_sum2(const float (&v)[2], uint32_t lane, uint32_t G) {
+  const uint32_t h = G >> 1;
+  const bool bh = (lane & h) != 0u;
+  float u = (bh ? v[1] : v[0]) + __shfl_xor_sync(0xffffffffu, bh ? v[0] : v[1], h);
+  for (uint32_t off = G >> 2; off > 0u; off >>= 1) u += __shfl_xor_sync(0xffffffffu, u, off);
   return u;
 }
 
-template <int FMT>
+// Row total from the row's group partials p[0..gpr) in the canonical order (tensor-
+// parallel row-parallel matrices; the plain order is p[0] + p[1] + ...): the row is `nseg` segments of
+// `spg` consecutive groups; each segment is summed left to right, then the segments in
+// a pairwise tree.  A segment is one tensor-parallel shard at the largest TP degree, so
+// a rank holding a power-of-two run of segments computes a complete subtree, and the
+// exchange that adds the ranks' results in the same pairwise tree (gather kernel)
+// reproduces the single-GPU sum bit for bit.
+__device__ __forceinline__ float row_total(const float* p, uint32_t gpr, uint32_t spg,
+                                        uint32_t nseg) {
+  (void)gpr;
+  float seg[8];
+#pragma unroll
+  for (uint32_t s = 0; s < 8u; ++s) {
+    if (s < nseg) {
+      float acc = p[s * spg];
+      for (uint32_t k = 1; k < spg; ++k) acc += p[s * spg + k];
+      seg[s] = acc;
+    }
+  }
+#pragma unroll
+  for (uint32_t step = 1; step < 8u; step <<= 1) {
+#pragma unroll
+    for (uint32_t i = 0; i + step < 8u; i += 2u * step) {
+      if (i + step < nseg) seg[i] += seg[i + step];
+    }
+  }
+  return seg[0];
+}
+
+// CANON: row sums in the canonical segment order (row_total) with lane groups of
+// a.group chunks; otherwise lane groups of 32 chunks reduce with the transposed
+// butterflies (red = 4 or 2) and narrower groups with group_sum.
+template <int FMT, bool CANON>
 __global__ void __launch_bounds__(544, 1) gemv_tiled_kernel(const GemvArgs a) {
   constexpr uint32_t PB = FmtTraits<FMT>::payload_bytes;
   constexpr uint32_t MB = FmtTraits<FMT>::meta_bytes;
@@ -438,6 +471,7 @@ __global__ void __launch_bounds__(544, 1) gemv_tiled_kernel(const GemvArgs a) {
   const bool leader = valid && (c & (a.group - 1u)) == 0u;
   const uint32_t row_stride = bpr * PB, meta_stride = bpr * MB;
   const uint32_t Q = a.stage_rows / a.rpp;
+  const uint32_t G = CANON ? a.group : 32u;
 
   const IqTables tables = iq_tables<FMT>(smem + a.table_off, tid & 31u);
   pdl_wait();  // x / act / residual / token come from the previous kernel
@@ -466,7 +500,7 @@ __global__ void __launch_bounds__(544, 1) gemv_tiled_kernel(const GemvArgs a) {
       const uint8_t* st = stages + s * a.stage_bytes;
       const uint32_t lr0 = j * a.stage_rows + slot;  // tile row of q = 0
       if (a.red == 4u) {
-        // A warp covers 32 chunks of one row slot: four passes' chunks, then one
+        // Each lane group covers G chunks of one row slot: four passes' chunks, then one
         // transposed reduction for the four rows.
         for (uint32_t q = 0; q < Q; q += 4u) {
           float v[4];
@@ -480,9 +514,9 @@ __global__ void __launch_bounds__(544, 1) gemv_tiled_kernel(const GemvArgs a) {
                                     xr, tables);
             }
           }
-          const float u = warp_sum4(v, lane);
-          const uint32_t lr = lr0 + (q + (((lane >> 2) & 2u) | ((lane >> 4) & 1u))) * a.rpp;
-          if ((lane & 7u) == 0u && valid && lr < nrows && !failed) rb[lr * gpr + gidx] = u;
+          const float u = warp_sum4(v, lane, G);
+          const uint32_t lr = lr0 + (q + ((lane & (G >> 2)) ? 2u : 0u) + ((lane & (G >> 1)) ? 1u : 0u)) * a.rpp;
+          if ((lane & ((G >> 2) - 1u)) == 0u && valid && lr < nrows && !failed) rb[lr * gpr + gidx] = u;
         }
       } else if (a.red == 2u) {
         for (uint32_t q = 0; q < Q; q += 2u) {
@@ -497,9 +531,9 @@ __global__ void __launch_bounds__(544, 1) gemv_tiled_kernel(const GemvArgs a) {
                                     xr, tables);
             }
           }
-          const float u = warp_sum2(v, lane);
-          const uint32_t lr = lr0 + (q + (lane >> 4)) * a.rpp;
-          if ((lane & 15u) == 0u && valid && lr < nrows && !failed) rb[lr * gpr + gidx] = u;
+          const float u = warp_sum2(v, lane, G);
+          const uint32_t lr = lr0 + (q + ((lane & (G >> 1)) ? 1u : 0u)) * a.rpp;
+          if ((lane & ((G >> 1) - 1u)) == 0u && valid && lr < nrows && !failed) rb[lr * gpr + gidx] = u;
         }
       }
 #pragma unroll 2
@@ -524,10 +558,15 @@ __global__ void __launch_bounds__(544, 1) gemv_tiled_kernel(const GemvArgs a) {
     }
     consumer_sync(nconsumers);
     for (uint32_t t = tid; t < nrows; t += nconsumers) {
-      float v = 0.f;
-      for (uint32_t k = 0; k < gpr; ++k) v += rb[t * gpr + k];
+      float v;
+      if constexpr (CANON) {
+        v = row_total(rb + t * gpr, gpr, a.canon_spg, a.canon_nseg);
+      } else {
+        v = 0.f;
+        for (uint32_t k = 0; k < gpr; ++k) v += rb[t * gpr + k];
+      }
       const uint32_t row = row0 + t;
-      if (a.residual != nullptr) v += a.residual[row];
+      if (a.residual != nullptr) v = a.residual[row] + v;
       g.y[row] = v;
       if (a.ex.n != 0u) {  // NVLink peer stores of (epoch, value)
         const uint64_t word = (static_cast<uint64_t>(ex_epoch) << 32) | __float_as_uint(v);
@@ -614,7 +653,7 @@ uint32_t resident_ctas(K kernel, uint32_t threads, uint32_t smem) {
   return static_cast<uint32_t>(n);
 }
 
-void fill_args(GemvArgs& a, const GemvPlan& plan) {
+void fill_args(GemvArgs& a, const GemvPlan& plan, bool canon = false) {
   a.group = plan.group;
   a.rpp = plan.rpp;
   a.passes = plan.passes;
@@ -630,7 +669,7 @@ void fill_args(GemvArgs& a, const GemvPlan& plan) {
   a.stage_mask = plan.stage_passes - 1u;
   a.stage_shift = static_cast<uint32_t>(__builtin_ctz(plan.stage_passes));
   a.red = 0u;
-  if (plan.tiled != 0u && plan.group == 32u) {
+  if (plan.tiled != 0u && (plan.group == 32u || (canon && plan.group >= 4u))) {
     a.red = (plan.stage_passes & 3u) == 0u ? 4u : (plan.stage_passes & 1u) == 0u ? 2u : 0u;
   }
 }
@@ -653,11 +692,11 @@ cudaError_t launch_gemv_fmt(GemvArgs a, cudaStream_t stream) {
       a.tma_ok = 1u;
       a.nseg = 1u;
       a.seg[0] = GemvSeg{a.payload, a.meta, a.y, a.rows, plan.num_tiles};
-      const cudaError_t e = ensure_smem_attr(gemv_tiled_kernel<FMT>, dev.max_smem_optin);
+      const cudaError_t e = ensure_smem_attr(gemv_tiled_kernel<FMT, false>, dev.max_smem_optin);
       if (e != cudaSuccess) return e;
-      const uint32_t per_sm = resident_ctas(gemv_tiled_kernel<FMT>, plan.threads, plan.smem_bytes);
+      const uint32_t per_sm = resident_ctas(gemv_tiled_kernel<FMT, false>, plan.threads, plan.smem_bytes);
       const uint32_t grid = std::max(1u, std::min(plan.num_tiles, per_sm * dev.sms));
-      return launch_k(gemv_tiled_kernel<FMT>, grid, plan.threads, plan.smem_bytes, stream, a);
+      return launch_k(gemv_tiled_kernel<FMT, false>, grid, plan.threads, plan.smem_bytes, stream, a);
     }
   }
   // Unaligned packs (or shapes the tiled plan cannot stage): all-thread copies.
@@ -718,11 +757,11 @@ cudaError_t launch_multi_fmt(GemvArgs a, uint32_t nseg, const GemvSeg* segs, cud
   a.meta = segs[0].meta;
   a.y = segs[0].y;
   a.rows = segs[0].rows;
-  const cudaError_t e = ensure_smem_attr(gemv_tiled_kernel<FMT>, dev.max_smem_optin);
+  const cudaError_t e = ensure_smem_attr(gemv_tiled_kernel<FMT, false>, dev.max_smem_optin);
   if (e != cudaSuccess) return e;
-  const uint32_t per_sm = resident_ctas(gemv_tiled_kernel<FMT>, plan.threads, plan.smem_bytes);
+  const uint32_t per_sm = resident_ctas(gemv_tiled_kernel<FMT, false>, plan.threads, plan.smem_bytes);
   const uint32_t grid = std::max(1u, std::min(tiles, per_sm * dev.sms));
-  return launch_k(gemv_tiled_kernel<FMT>, grid, plan.threads, plan.smem_bytes, stream, a);
+  return launch_k(gemv_tiled_kernel<FMT, false>, grid, plan.threads, plan.smem_bytes, stream, a);
 }
 
 // Threads per CTA: rows-per-pass is the smallest multiple of 32/group (whole warps)
@@ -750,8 +789,8 @@ constexpr uint32_t kThreads = QG_THREADS;
 constexpr uint32_t kSmemOptinMax = 232448u;
 constexpr uint32_t kIqStageBudget = QG_IQ_STAGE_BUDGET;
 
-void plan_threads(uint32_t tpr, GemvPlan& p, uint32_t limit = 256u) {
-  p.group = gcd_u32(tpr, 32u);
+void plan_threads(uint32_t tpr, GemvPlan& p, uint32_t limit = 256u, uint32_t group_cap = 32u) {
+  p.group = gcd_u32(tpr, group_cap);
   const uint32_t base = 32u / p.group;
   uint32_t rpp = base;
   if (rpp * tpr > 512u) rpp = 1u;
@@ -811,14 +850,14 @@ uint32_t balanced_passes(uint32_t total_passes, uint32_t q, uint32_t sms, uint32
 // Plan of the tiled kernel.  Stage = Q passes of ~16 KB whose byte count is a multiple
 // of 16 (IQ formats: at least four passes); S stages within ~96 KB (2..8); tiles of P
 // passes (Q | P) balanced over the SMs (balanced_passes).
-GemvPlan plan_gemv(int fmt, uint32_t rows, uint32_t cols, int sms) {
+GemvPlan plan_gemv(int fmt, uint32_t rows, uint32_t cols, int sms, uint32_t group_cap) {
   GemvPlan p{};
   sms = std::max(sms, 1);  // no device (host-side plan query): plan for one SM
   const uint32_t PB = qg_payload_bytes_per_block(fmt);
   const uint32_t MB = qg_meta_bytes_per_block(fmt);
   const uint32_t bpr = cols >> 8, tpr = cols / 64u;
   const bool iq = iq_table_bytes(fmt) != 0u;
-  plan_threads(tpr, p, iq ? kIqThreads : kThreads);
+  plan_threads(tpr, p, iq ? kIqThreads : kThreads, group_cap);
   const uint32_t row_bytes = bpr * PB, row_meta = bpr * MB;
   // Stage: smallest power-of-two passes with 16-B aligned bytes, grown toward 16 KB.
   uint32_t q = 1u;
@@ -834,7 +873,8 @@ GemvPlan plan_gemv(int fmt, uint32_t rows, uint32_t cols, int sms) {
   while (q < 16u && 2u * q * p.rpp * (row_bytes + row_meta) <= stage_target) q <<= 1;
   // IQ readers are issue-bound: four passes per stage give every thread four
   // independent chunks and one transposed reduction per four rows.
-  if (p.group == 32u) q = std::max(q, iq ? kIqStagePasses : kStagePasses);
+  // (Canonical-order plans, group_cap < 32, keep the same four passes.)
+  if (p.group == 32u || group_cap < 32u) q = std::max(q, iq ? kIqStagePasses : kStagePasses);
   const uint32_t total_passes = std::max(1u, (rows + p.rpp - 1u) / p.rpp);
   // Small matrices: a stage is never more passes than the matrix has (but never less
   // than its 16-B aligned size).
@@ -930,8 +970,12 @@ cudaError_t launch_gemv(int fmt, const uint8_t* payload, const uint8_t* meta, co
 }
 
 namespace {
+// Tiled launch whose row sums follow the canonical segment order (canon.seg_chunks
+// 64-column chunks per segment, a multiple of 4, so lane groups are at least 4 wide;
+// canon.nseg segments per row), optionally exchanging the rows with the other ranks.  cudaErrorNotSupported when the shape, the alignment or
+// the segment size does not allow the tiled kernel.
 template <int FMT>
-cudaError_t launch_exchange_fmt(GemvArgs a, cudaStream_t stream) {
+cudaError_t launch_canon_fmt(GemvArgs a, const GemvCanon& canon, cudaStream_t stream) {
   constexpr uint32_t MB = FmtTraits<FMT>::meta_bytes;
   const DeviceInfo dev = device_info();
   a.tpr = a.cols / 64u;
@@ -939,26 +983,47 @@ cudaError_t launch_exchange_fmt(GemvArgs a, cudaStream_t stream) {
   const bool aligned = (reinterpret_cast<uintptr_t>(a.payload) & 15u) == 0u &&
                        (MB == 0u || (reinterpret_cast<uintptr_t>(a.meta) & 15u) == 0u);
   if (a.cols < 256u || a.tpr > 512u || !aligned) return cudaErrorNotSupported;
-  const GemvPlan plan = plan_gemv(FMT, a.rows, a.cols, dev.sms);
-  if (!plan.tiled || plan.smem_bytes > static_cast<uint32_t>(dev.max_smem_optin)) {
+  if (canon.nseg == 0u || canon.nseg > 8u || (canon.nseg & (canon.nseg - 1u)) != 0u ||
+      canon.seg_chunks % 4u != 0u || canon.seg_chunks == 0u || canon.seg_chunks * canon.nseg != a.tpr) {
+    return cudaErrorInvalidValue;
+  }
+  const uint32_t cg = gcd_u32(canon.seg_chunks, 32u);
+  const GemvPlan plan = plan_gemv(FMT, a.rows, a.cols, dev.sms, cg);
+  if (!plan.tiled || plan.smem_bytes > static_cast<uint32_t>(dev.max_smem_optin) || plan.group != cg) {
     return cudaErrorNotSupported;
   }
-  fill_args(a, plan);
+  fill_args(a, plan, true);
   a.tma_ok = 1u;
   a.nseg = 1u;
   a.seg[0] = GemvSeg{a.payload, a.meta, a.y, a.rows, plan.num_tiles};
-  const cudaError_t e = ensure_smem_attr(gemv_tiled_kernel<FMT>, dev.max_smem_optin);
+  a.canon_spg = canon.seg_chunks / cg;
+  a.canon_nseg = canon.nseg;
+  const cudaError_t e = ensure_smem_attr(gemv_tiled_kernel<FMT, true>, dev.max_smem_optin);
   if (e != cudaSuccess) return e;
-  const uint32_t per_sm = resident_ctas(gemv_tiled_kernel<FMT>, plan.threads, plan.smem_bytes);
+  const uint32_t per_sm = resident_ctas(gemv_tiled_kernel<FMT, true>, plan.threads, plan.smem_bytes);
   const uint32_t grid = std::max(1u, std::min(plan.num_tiles, per_sm * dev.sms));
-  return launch_k(gemv_tiled_kernel<FMT>, grid, plan.threads, plan.smem_bytes, stream, a);
+  return launch_k(gemv_tiled_kernel<FMT, true>, grid, plan.threads, plan.smem_bytes, stream, a);
+}
+
+cudaError_t launch_canon(int fmt, const GemvArgs& a, const GemvCanon& canon, cudaStream_t stream) {
+  switch (fmt) {
+    case QG_FMT_Q4K_RAW: return launch_canon_fmt<QG_FMT_Q4K_RAW>(a, canon, stream);
+    case QG_FMT_Q4K_SPLIT_PREDECODED: return launch_canon_fmt<QG_FMT_Q4K_SPLIT_PREDECODED>(a, canon, stream);
+    case QG_FMT_Q4K_SPLIT_HALF: return launch_canon_fmt<QG_FMT_Q4K_SPLIT_HALF>(a, canon, stream);
+    case QG_FMT_Q4K_SPLIT_COMPACT: return launch_canon_fmt<QG_FMT_Q4K_SPLIT_COMPACT>(a, canon, stream);
+    case QG_FMT_Q4K_SPLIT_NATIVE: return launch_canon_fmt<QG_FMT_Q4K_SPLIT_NATIVE>(a, canon, stream);
+    case QG_FMT_Q5K: return launch_canon_fmt<QG_FMT_Q5K>(a, canon, stream);
+    case QG_FMT_IQ2S: return launch_canon_fmt<QG_FMT_IQ2S>(a, canon, stream);
+    case QG_FMT_IQ3S: return launch_canon_fmt<QG_FMT_IQ3S>(a, canon, stream);
+    default: return cudaErrorInvalidValue;
+  }
 }
 }  // namespace
 
 cudaError_t launch_gemv_exchange(int fmt, const uint8_t* payload, const uint8_t* meta,
                                  const float* x, const void* act, float* y, const float* residual,
                                  uint32_t rows, uint32_t cols, const GemvExchange& ex,
-                                 cudaStream_t stream) {
+                                 const GemvCanon& canon, cudaStream_t stream) {
   if (ex.n == 0u || ex.n > kMaxExchangeRanks || ex.epoch == nullptr) {
     return cudaErrorInvalidValue;
   }
@@ -972,17 +1037,23 @@ cudaError_t launch_gemv_exchange(int fmt, const uint8_t* payload, const uint8_t*
   a.rows = rows;
   a.cols = cols;
   a.ex = ex;
-  switch (fmt) {
-    case QG_FMT_Q4K_RAW: return launch_exchange_fmt<QG_FMT_Q4K_RAW>(a, stream);
-    case QG_FMT_Q4K_SPLIT_PREDECODED: return launch_exchange_fmt<QG_FMT_Q4K_SPLIT_PREDECODED>(a, stream);
-    case QG_FMT_Q4K_SPLIT_HALF: return launch_exchange_fmt<QG_FMT_Q4K_SPLIT_HALF>(a, stream);
-    case QG_FMT_Q4K_SPLIT_COMPACT: return launch_exchange_fmt<QG_FMT_Q4K_SPLIT_COMPACT>(a, stream);
-    case QG_FMT_Q4K_SPLIT_NATIVE: return launch_exchange_fmt<QG_FMT_Q4K_SPLIT_NATIVE>(a, stream);
-    case QG_FMT_Q5K: return launch_exchange_fmt<QG_FMT_Q5K>(a, stream);
-    case QG_FMT_IQ2S: return launch_exchange_fmt<QG_FMT_IQ2S>(a, stream);
-    case QG_FMT_IQ3S: return launch_exchange_fmt<QG_FMT_IQ3S>(a, stream);
-    default: return cudaErrorInvalidValue;
-  }
+  return launch_canon(fmt, a, canon, stream);
+}
+
+cudaError_t launch_gemv_canonical(int fmt, const uint8_t* payload, const uint8_t* meta,
+                                  const float* x, const void* act, float* y, const float* residual,
+                                  uint32_t rows, uint32_t cols, const GemvCanon& canon,
+                                  cudaStream_t stream) {
+  GemvArgs a{};
+  a.payload = payload;
+  a.meta = meta;
+  a.x = x;
+  a.xq = static_cast<const ActChunk*>(act);
+  a.y = y;
+  a.residual = residual;
+  a.rows = rows;
+  a.cols = cols;
+  return launch_canon(fmt, a, canon, stream);
 }
 
 cudaError_t launch_gemv_multi(int fmt, uint32_t nseg, const uint8_t* const* payload,

@@ -51,7 +51,8 @@ struct GemvPlan {
 };
 
 // Tiled (TMA-pipelined) plan; .tiled == 0 when the shape cannot be staged that way.
-GemvPlan plan_gemv(int fmt, uint32_t rows, uint32_t cols, int sms);
+// Row sums reduce lane groups of gcd(cols / 64, group_cap) chunks.
+GemvPlan plan_gemv(int fmt, uint32_t rows, uint32_t cols, int sms, uint32_t group_cap = 32u);
 // Plan of the all-thread-copy kernel used for packs that are not 16-B aligned.
 GemvPlan plan_staged(int fmt, uint32_t rows, uint32_t cols, int sms);
 
@@ -91,19 +92,35 @@ cudaError_t launch_weighted_rmsnorm(const float* x, const float* w, uint32_t n, 
 cudaError_t launch_silu_gate(const float* gate, const float* up, uint32_t n, float* h,
                              cudaStream_t stream);
 
-// h = x * inv_rms(x) * w (+ h's prepared activation); one CTA.
-// y = W x whose rows are also exchanged to every rank (tiled kernel only; returns
+// Canonical summation order of a row-parallel matrix's rows: the full row (all ranks'
+// columns) is 8 (or fewer, a power of two) segments, one tensor-parallel shard at the
+// largest degree each; a rank's launch covers `nseg` consecutive segments of
+// `seg_chunks` 64-column chunks.  Each segment is summed in a fixed order, the segments
+// in a pairwise tree, and the exchange gather adds the ranks in the same tree, so every
+// tensor-parallel degree produces the single-GPU row sums bit for bit.
+struct GemvCanon {
+  uint32_t seg_chunks;
+  uint32_t nseg;
+};
+
+// y = W x (+ residual) with canonical row sums (tiled kernel only; returns
 // cudaErrorNotSupported for shapes or alignments that need the fallback kernels).
+cudaError_t launch_gemv_canonical(int fmt, const uint8_t* payload, const uint8_t* meta,
+                                  const float* x, const void* act, float* y, const float* residual,
+                                  uint32_t rows, uint32_t cols, const GemvCanon& canon,
+                                  cudaStream_t stream);
+// The same, whose rows are also exchanged to every rank.
 cudaError_t launch_gemv_exchange(int fmt, const uint8_t* payload, const uint8_t* meta,
                                  const float* x, const void* act, float* y, const float* residual,
                                  uint32_t rows, uint32_t cols, const GemvExchange& ex,
-                                 cudaStream_t stream);
-// Reads every rank's slot, waiting (bounded) for each word of epoch+1, sums the ranks in
-// rank order into x_out, advances the epoch, then RMSNorm*w and h's int8 planes like
-// launch_norm_prepare.
+                                 const GemvCanon& canon, cudaStream_t stream);
+// Reads every rank's slot, waiting (bounded) for each word of epoch+1, adds the ranks in
+// a pairwise tree and then to `residual` (optional) into x_out, advances the epoch, then
+// RMSNorm*w and h's int8 planes like launch_norm_prepare.
 cudaError_t launch_gather_norm_prepare(const uint64_t* buf, uint32_t* epoch, uint32_t nsrc,
-                                       uint32_t stride, const float* w, uint32_t n, float eps,
-                                       float* x_out, float* h, void* act, cudaStream_t stream);
+                                       uint32_t stride, const float* residual, const float* w,
+                                       uint32_t n, float eps, float* x_out, float* h, void* act,
+                                       cudaStream_t stream);
 cudaError_t launch_norm_prepare(const float* x, const float* w, uint32_t n, float eps, float* h,
                                 void* act, cudaStream_t stream);
 // a = silu(gate) * up (+ a's prepared activation).

@@ -5,8 +5,9 @@
   small sizes; `rank_weights(model, rank, tp)` cuts one rank's shards out of it the
   way the decoder expects them (row shards of Wq/Wk/Wv/Wg/Wu/head, column shards of
   Wo/Wd on 256-column block boundaries, the rank's kv heads of the cache).
-* `synthetic_rank_weights(spec, rank, tp, ...)` -- the same shard shapes drawn
-  directly on the GPU (full-size benchmark: ~31 GB of packs at tp=1).
+* `synthetic_rank_weights(spec, rank, tp, ...)` -- one seeded global model drawn
+  directly on the GPU, cut into the same shard shapes (full-size benchmark: ~31 GB of
+  packs at tp=1); identical weights at every tensor-parallel degree.
 * `Decoder` -- one rank's qg_decoder plus its workspace.
 """
 
@@ -79,8 +80,8 @@ class DecoderLayerC(ctypes.Structure):
                 + [("k_cache", c_void_p), ("v_cache", c_void_p)])
 
 
-COLLECTIVE_NVLINK = 0  # all-reduces fused into the GEMVs over NVLink peer memory
-COLLECTIVE_NCCL = 1    # ncclAllReduce between the kernels
+COLLECTIVE_NVLINK = 0  # exchanges fused into the GEMVs over NVLink peer memory
+COLLECTIVE_NCCL = 1    # the same exchange words moved by ncclAllGather between the kernels
 
 
 def dims_struct(spec: ModelSpec, rank: int, tp: int, collective: int = COLLECTIVE_NVLINK) -> DecoderDims:
@@ -182,29 +183,74 @@ def _gpu_pack(fmt: int, rows: int, cols: int, gen: torch.Generator, device) -> t
     return payload.view(-1), None
 
 
-def synthetic_rank_weights(spec: ModelSpec, rank: int, tp: int, device, seed: int = 0) -> dict:
-    """This rank's shards drawn directly on the GPU (shapes as rank_weights)."""
+def _rows_view(p: tuple, fmt: int, cols: int, r0: int, r1: int) -> tuple:
+    payload, _ = p
+    row = (cols // 256) * packs.payload_bytes_per_block(fmt)
+    return payload.view(-1, row)[r0:r1].reshape(-1), None
+
+
+def _cols_copy(p: tuple, fmt: int, rows: int, cols: int, c0: int, c1: int) -> tuple:
+    payload, _ = p
+    pb = packs.payload_bytes_per_block(fmt)
+    blocks = payload.view(rows, cols // 256, pb)[:, c0 // 256: c1 // 256, :]
+    return blocks.contiguous().view(-1), None
+
+
+def synthetic_rank_weights(spec: ModelSpec, rank: int, tp: int, device, seed: int = 0,
+                           keep_full: bool = False) -> dict:
+    """This rank's shards (shapes as rank_weights) of one seeded global model drawn on the
+    GPU: every rank draws the same global tensors in the same order from a generator with
+    the same seed and keeps its own rows / columns / kv heads, so the shards of every
+    tensor-parallel degree are cut from identical weights (the step is comparable across
+    degrees).  With keep_full the global weights are returned as well (`full`, the tp=1
+    shards; the rank's shards are then views into them where they are contiguous)."""
     sh = shard_shape(spec, rank, tp)
     gen = torch.Generator(device=device)
-    gen.manual_seed(seed * 7919 + rank)
+    gen.manual_seed(seed * 7919 + 17)
     q, kv, f = sh["q_rows"], sh["kv_rows"], sh["ffn_rows"]
-    shapes = dict(wq=(spec.attn_fmt, q, spec.hidden), wk=(spec.attn_fmt, kv, spec.hidden),
-                  wv=(spec.attn_fmt, kv, spec.hidden), wo=(spec.attn_fmt, spec.hidden, q),
-                  wg=(spec.ffn_fmt, f, spec.hidden), wu=(spec.ffn_fmt, f, spec.hidden),
-                  wd=(spec.down_fmt, spec.hidden, f))
-    layers = []
+    q0, k0, f0 = rank * q, rank * kv, rank * f
+    h0, h1 = rank * (spec.n_kv_heads // tp), (rank + 1) * (spec.n_kv_heads // tp)
+    full_shapes = dict(wq=(spec.attn_fmt, spec.q_rows, spec.hidden),
+                       wk=(spec.attn_fmt, spec.kv_rows, spec.hidden),
+                       wv=(spec.attn_fmt, spec.kv_rows, spec.hidden),
+                       wo=(spec.attn_fmt, spec.hidden, spec.q_rows),
+                       wg=(spec.ffn_fmt, spec.ffn, spec.hidden),
+                       wu=(spec.ffn_fmt, spec.ffn, spec.hidden),
+                       wd=(spec.down_fmt, spec.hidden, spec.ffn))
+    row_cut = dict(wq=(q0, q0 + q), wk=(k0, k0 + kv), wv=(k0, k0 + kv), wg=(f0, f0 + f), wu=(f0, f0 + f))
+    col_cut = dict(wo=(q0, q0 + q), wd=(f0, f0 + f))
+    layers, full_layers = [], []
     for _ in range(spec.layers):
         L = {"attn_norm": 1 + 0.02 * torch.randn(spec.hidden, device=device, generator=gen),
              "ffn_norm": 1 + 0.02 * torch.randn(spec.hidden, device=device, generator=gen)}
-        for n, (fmt, r, c) in shapes.items():
-            L[n] = _gpu_pack(fmt, r, c, gen, device)
-        cache = (spec.n_kv_heads // tp, spec.ctx_max, spec.head_dim)
-        L["k_cache"] = torch.randn(cache, device=device, generator=gen).half()
-        L["v_cache"] = torch.randn(cache, device=device, generator=gen).half()
+        F = dict(L)
+        for n, (fmt, r, c) in full_shapes.items():
+            full = _gpu_pack(fmt, r, c, gen, device)
+            F[n] = full
+            if n in row_cut:
+                part = _rows_view(full, fmt, c, *row_cut[n])
+                L[n] = part if keep_full else (part[0].clone(), None)
+            else:
+                L[n] = _cols_copy(full, fmt, r, c, *col_cut[n])
+        cache = (spec.n_kv_heads, spec.ctx_max, spec.head_dim)
+        kc = torch.randn(cache, device=device, generator=gen).half()
+        vc = torch.randn(cache, device=device, generator=gen).half()
+        F["k_cache"], F["v_cache"] = kc, vc
+        L["k_cache"] = kc[h0:h1] if keep_full else kc[h0:h1].clone()
+        L["v_cache"] = vc[h0:h1] if keep_full else vc[h0:h1].clone()
         layers.append(L)
+        if keep_full:
+            full_layers.append(F)
     final_norm = 1 + 0.02 * torch.randn(spec.hidden, device=device, generator=gen)
-    head = _gpu_pack(spec.head_fmt, sh["vocab_rows"], spec.hidden, gen, device)
-    return dict(layers=layers, final_norm=final_norm, head=head, shard=sh, on_device=True)
+    head_full = _gpu_pack(spec.head_fmt, spec.vocab, spec.hidden, gen, device)
+    v0 = sh["vocab_offset"]
+    head = _rows_view(head_full, spec.head_fmt, spec.hidden, v0, v0 + sh["vocab_rows"])
+    out = dict(layers=layers, final_norm=final_norm,
+               head=head if keep_full else (head[0].clone(), None), shard=sh, on_device=True)
+    if keep_full:
+        out["full"] = dict(layers=full_layers, final_norm=final_norm, head=head_full,
+                           shard=shard_shape(spec, 0, 1), on_device=True)
+    return out
 
 
 # --------------------------------------------------------------------------- runtime

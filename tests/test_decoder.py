@@ -19,6 +19,9 @@ SMALL = dict(layers=2, hidden=512, n_q_heads=4, n_kv_heads=2, head_dim=128, ffn=
 # a model that shards four ways (every rank: 2 q heads, 1 kv head, 512 ffn rows, 256 vocab rows)
 SMALL_TP4 = dict(layers=2, hidden=1024, n_q_heads=8, n_kv_heads=4, head_dim=128, ffn=2048,
                  vocab=1024, ctx_max=64)
+# eight ways (every rank: 2 q heads, 1 kv head, 256 ffn rows, 128 vocab rows)
+SMALL_TP8 = dict(layers=2, hidden=1024, n_q_heads=16, n_kv_heads=8, head_dim=128, ffn=2048,
+                 vocab=1024, ctx_max=64)
 
 
 def _oracle(port, model, x, pos):
@@ -95,25 +98,10 @@ def test_decoder_graph_replay_matches_eager(cuda):
 TP_STEPS = (30, 31, 32)  # positions; the middle step runs as a captured graph
 
 
-def _tp_rank(rank, world, q_in, q_out, spec_kw):
-    sys.path.insert(0, str(REPO / "local-ai-gpu-acceleration_b200"))
-    import torch
-
-    from qgemv_b200 import decoder, packs
+def _run_steps(dec, spec, dev):
+    from qgemv_b200 import packs
     from qgemv_b200.slice import StepGraph
 
-    torch.cuda.set_device(rank)
-    spec = decoder.ModelSpec(**spec_kw)
-    model = decoder.HostModel.synthetic(spec, seed=21)
-    if rank == 0:
-        nid = decoder.nccl_unique_id()
-        for _ in range(world - 1):
-            q_in.put(nid)
-    else:
-        nid = q_in.get(timeout=120)
-    dev = f"cuda:{rank}"
-    dec = decoder.Decoder(spec, decoder.rank_weights(model, rank, world), rank=rank, tp=world,
-                          nccl_id=nid, device=dev)
     out = []
     for i, pos in enumerate(TP_STEPS):
         x = torch.from_numpy(packs.synthetic_activation(spec.hidden, 22 + i)).to(dev)
@@ -129,15 +117,41 @@ def _tp_rank(rank, world, q_in, q_out, spec_kw):
             tok = int(dec.step(x, pos).item())
         torch.cuda.synchronize()
         out.append((tok, dec.hidden().cpu().numpy()))
-    q_out.put((rank, out))
+    return out
+
+
+def _tp_rank(rank, world, q_in, q_out, spec_kw, collective):
+    sys.path.insert(0, str(REPO / "local-ai-gpu-acceleration_b200"))
+    import torch
+
+    from qgemv_b200 import decoder, ops
+
+    torch.cuda.set_device(rank)
+    spec = decoder.ModelSpec(**spec_kw)
+    model = decoder.HostModel.synthetic(spec, seed=21)
+    if rank == 0:
+        nid = decoder.nccl_unique_id()
+        for _ in range(world - 1):
+            q_in.put(nid)
+    else:
+        nid = q_in.get(timeout=120)
+    dev = f"cuda:{rank}"
+    dec = decoder.Decoder(spec, decoder.rank_weights(model, rank, world), rank=rank, tp=world,
+                          nccl_id=nid, device=dev, collective=collective)
+    out = _run_steps(dec, spec, dev)
+    q_out.put((rank, out, ops.get_error()))
     dec.close()
 
 
-@pytest.mark.parametrize("world,spec_kw", [(2, SMALL), (4, SMALL_TP4)], ids=["tp2", "tp4"])
-def test_decoder_tp_matches_oracle(port, world, spec_kw):
-    """World ranks over NVLink (fused exchange in the Wo / Wd GEMVs, NCCL only for the
-    token all-gather): three consecutive steps -- eager, captured graph, eager -- against
-    the oracle stepping the same model with its caches carried along."""
+@pytest.mark.parametrize("world,spec_kw,collective", [
+    (2, SMALL, 0), (2, SMALL, 1), (4, SMALL_TP4, 0), (8, SMALL_TP8, 0)],
+    ids=["tp2", "tp2-nccl", "tp4", "tp8"])
+def test_decoder_tp_matches_oracle_and_tp1(port, world, spec_kw, collective):
+    """World ranks over NVLink (exchange fused into the Wo / Wd GEMVs; or, tp2-nccl, the
+    same exchange words moved by ncclAllGather): three consecutive steps -- eager, captured
+    graph, eager -- against the oracle stepping the same model with its caches carried
+    along, and bit for bit against the same three steps on one GPU (TP 1): the token and
+    every bit of the hidden state on every rank."""
     if not torch.cuda.is_available() or torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     sys.path.insert(0, str(REPO / "oracle"))
@@ -154,17 +168,24 @@ def test_decoder_tp_matches_oracle(port, world, spec_kw):
     ctx = mp.get_context("spawn")
     q_in, q_out = ctx.Queue(), ctx.Queue()
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
-    procs = [ctx.Process(target=_tp_rank, args=(r, world, q_in, q_out, spec_kw)) for r in range(world)]
+    procs = [ctx.Process(target=_tp_rank, args=(r, world, q_in, q_out, spec_kw, collective))
+             for r in range(world)]
     for p in procs:
         p.start()
     res = [q_out.get(timeout=300) for _ in procs]
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
-    for _, steps in res:
+    for _, steps, err in res:
+        assert err == 0
         for (tok, hid), (want_tok, want_hidden) in zip(steps, want):
             _check(hid, want_hidden, tok, want_tok)
-    # every rank holds the same bits of the replicated hidden state
-    for _, other in res[1:]:
-        for (_, a), (_, b) in zip(res[0][1], other):
-            assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+    # TP 1 on cuda:0, the same model, steps and caches
+    dec1 = decoder.Decoder(spec, decoder.rank_weights(model, 0, 1), device="cuda:0")
+    single = _run_steps(dec1, spec, "cuda:0")
+    dec1.close()
+    for rank, steps, _ in res:
+        for k, ((tok, hid), (tok1, hid1)) in enumerate(zip(steps, single)):
+            assert tok == tok1, f"rank {rank} step {k}: token {tok} vs TP1 {tok1}"
+            assert np.array_equal(hid.view(np.uint32), hid1.view(np.uint32)), \
+                f"rank {rank} step {k}: hidden state differs from TP1"
