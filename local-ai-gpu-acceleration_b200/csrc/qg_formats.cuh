@@ -305,25 +305,19 @@ __device__ __forceinline__ void q4_nibble_dot(const uint4 q0, const uint4 q1, co
 //  * C3 = kIq3Copies copies of a 4-byte table (IQ3_S grid): word (e*C3 + lane % C3);
 //    with 32 copies every lane owns a bank (conflict-free), with 16 lanes k and k+16
 //    share one (at most a 2-way conflict);
-//  * 16 copies of an 8-byte table (sign masks): entry (e*16 + k) sits in bank pair k,
-//    one bank pair per lane of a half-warp -> conflict-free;
-//  * C = kIq2Copies copies of the 8-byte IQ2_S expanded grid: copy r = k % C occupies
+//  * 16 copies of an 8-byte table (IQ3_S sign masks): entry (e*16 + k) sits in bank pair
+//    k, one bank pair per lane of a half-warp -> conflict-free;
+//  * C = kIq2Copies copies of the 8-byte IQ2_S grid (bytes 2k+1): copy r = k % C occupies
 //    only the bank pairs r + C*i, so 16/C lanes of a half-warp compete for 16/C pairs.
-// The pointers are already offset to this lane's copy, so a lookup is one shifted add:
-// kgrid2[C e], sign2[16 e], grid3[C3 e], sign3[16 e].
+// The pointers are already offset to this lane's copy, so a lookup is one multiply-add:
+// kgrid2[C e], grid3[C3 e], sign3[16 e].
 #ifndef QG_IQ2S_KGRID_COPIES
 #define QG_IQ2S_KGRID_COPIES 8u
 #endif
 constexpr uint32_t kIq2Copies = QG_IQ2S_KGRID_COPIES;
 static_assert(kIq2Copies == 4u || kIq2Copies == 8u || kIq2Copies == 16u,
               "IQ2_S grid copies: 4, 8 or 16");
-// IQ2_S sign masks: from the shared table (0) or computed in registers (1, no table).
-#ifndef QG_IQ2S_ALU_SIGNS
-#define QG_IQ2S_ALU_SIGNS 1
-#endif
-constexpr bool kIq2AluSigns = QG_IQ2S_ALU_SIGNS != 0;
-constexpr uint32_t kIq2SignWord = 2048u * kIq2Copies;  // word offset of the IQ2_S sign table
-constexpr uint32_t kIq2TableBytes = (kIq2SignWord + (kIq2AluSigns ? 0u : 8192u)) * 4u;
+constexpr uint32_t kIq2TableBytes = 2048u * kIq2Copies * 4u;
 
 // Byte masks of four sign bits: byte i = 0xFF where bit i of s4 (< 16) is set.  The
 // multiply puts bit i at bit 8i + 7 (its four partial products do not overlap, so no
@@ -333,19 +327,50 @@ __device__ __forceinline__ uint32_t sign_bytes4(uint32_t s4) {
   asm("prmt.b32 %0, %1, 0, 0xBA98;" : "=r"(m) : "r"(s4 * 0x10204080u));
   return m;
 }
+// Four odd magnitudes (bytes) with the signs of s4's four bits applied (m ^ 0xFE = -m).
+__device__ __forceinline__ uint32_t apply_signs4(uint32_t mags, uint32_t s4) {
+  return mags ^ (sign_bytes4(s4) & 0xFEFEFEFEu);
+}
+// Byte g of `lo` in byte 0 and byte g of `hi` (< 128) in byte 1, zero above: the 16-bit
+// value lo_g + 256 hi_g in one prmt (the sign-replicating selector on hi's byte g, whose
+// top bit is clear, yields the zero bytes).
+template <int G>
+__device__ __forceinline__ uint32_t pair_bytes(uint32_t lo, uint32_t hi) {
+  constexpr uint32_t sel = G | ((4 + G) << 4) | ((8 | (4 + G)) << 8) | ((8 | (4 + G)) << 12);
+  uint32_t r;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(lo), "r"(hi), "n"(sel));
+  return r;
+}
+// The four 2-bit fields of a byte b, one per byte: byte g = (b >> 2g) & 3.  Fields 0, 2 and
+// fields 1, 3 are moved by two multiplies whose partial products do not overlap.
+__device__ __forceinline__ uint32_t spread2x4(uint32_t b) {
+  const uint32_t e = (b & 0x33u) * 0x1001u;      // field 0 -> bits 0-1, field 2 -> 16-17
+  const uint32_t o = (b & 0xCCu) * 0x40040u;     // field 1 -> bits 8-9, field 3 -> 24-25
+  return (e & 0x00030003u) | (o & 0x03000300u);
+}
+// The four bits of a nibble n, one per byte: byte i = bit i of n (positions 7j + i of the
+// four partial products are all distinct, so no carries).
+__device__ __forceinline__ uint32_t spread1x4(uint32_t n) {
+  return (n * 0x00204081u) & 0x01010101u;
+}
 #ifndef QG_IQ3S_GRID_COPIES
 #define QG_IQ3S_GRID_COPIES 32u
 #endif
 constexpr uint32_t kIq3Copies = QG_IQ3S_GRID_COPIES;
 static_assert(kIq3Copies == 16u || kIq3Copies == 32u, "IQ3_S grid copies: 16 or 32");
+// IQ3_S sign masks: computed in registers (0; measured 2% faster on B200 than the
+// table, whose 8-byte lookups add shared-memory wavefronts) or from a shared table (1).
+#ifndef QG_IQ3S_TABLE_SIGNS
+#define QG_IQ3S_TABLE_SIGNS 0
+#endif
+constexpr bool kIq3TableSigns = QG_IQ3S_TABLE_SIGNS != 0;
 constexpr uint32_t kIq3SignByte = 2048u * kIq3Copies;  // byte offset of the IQ3_S sign table
-constexpr uint32_t kIq3TableBytes = kIq3SignByte + 32768u;
+constexpr uint32_t kIq3TableBytes = kIq3SignByte + (kIq3TableSigns ? 32768u : 0u);
 
 struct IqTables {
-  const uint2* kgrid2;    // IQ2_S: 1024 entries x C copies (slot C e + k%C), 8 bytes 2k
-  const uint2* sign2;     // IQ2_S: 256 entries x 16 copies (slot 16e + k), bytes (sign ? 0x0E : 0)
+  const uint2* kgrid2;    // IQ2_S: 1024 entries x C copies (slot C e + k%C), 8 bytes 2k+1
   const uint32_t* grid3;  // IQ3_S: 512 entries x C3 copies (slot C3 e + lane%C3), 4 magnitudes
-  const uint2* sign3;     // IQ3_S: 256 entries x 16 copies (slot 16e + k), bytes (sign ? 0x1E : 0)
+  const uint2* sign3;     // IQ3_S: 256 entries x 16 copies (slot 16e + k), bytes (sign ? 0xFE : 0)
   uint32_t k;             // lane % 16
 };
 
@@ -464,6 +489,33 @@ __device__ __forceinline__ float chunk_dot<QG_FMT_Q5K>(const uint8_t* rp, const 
   return q4k_header_combine(h, g, sA, sB, x);
 }
 
+// One IQ2_S sub-block (32 weights, 4 groups of 8) against one half of x: the integer
+// sums of the two scale quarters (groups 0-1 with the low scale nibble, 2-3 with the
+// high), scaled by (2 nib + 1), into (h, l) for the x planes.
+__device__ __forceinline__ void iq2s_sub(uint32_t gl, uint32_t sg, uint32_t qhb, uint32_t scb,
+                                         const uint32_t* H, const uint32_t* L,
+                                         const IqTables& t, int& h, int& l) {
+  const uint32_t h4 = spread2x4(qhb);
+  uint32_t idx[4];
+  idx[0] = pair_bytes<0>(gl, h4);
+  idx[1] = pair_bytes<1>(gl, h4);
+  idx[2] = pair_bytes<2>(gl, h4);
+  idx[3] = pair_bytes<3>(gl, h4);
+  int ih[2] = {0, 0}, il[2] = {0, 0};
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    const uint2 k2 = t.kgrid2[idx[g] * kIq2Copies];
+    const uint32_t sb = sg >> (8 * g);
+    const uint32_t v0 = apply_signs4(k2.x, sb & 0x0fu);
+    const uint32_t v1 = apply_signs4(k2.y, (sb >> 4) & 0x0fu);
+    ih[g >> 1] = dp4a(v1, H[2 * g + 1], dp4a(v0, H[2 * g], ih[g >> 1]));
+    il[g >> 1] = dp4a(v1, L[2 * g + 1], dp4a(v0, L[2 * g], il[g >> 1]));
+  }
+  const int s0 = static_cast<int>(2u * (scb & 0x0fu) + 1u), s1 = static_cast<int>(2u * ((scb >> 4) & 0x0fu) + 1u);
+  h = s0 * ih[0] + s1 * ih[1];
+  l = s0 * il[0] + s1 * il[1];
+}
+
 template <>
 __device__ __forceinline__ float chunk_dot<QG_FMT_IQ2S>(const uint8_t* rp, const uint8_t*,
                                                         uint32_t c, const XChunk& x,
@@ -471,44 +523,52 @@ __device__ __forceinline__ float chunk_dot<QG_FMT_IQ2S>(const uint8_t* rp, const
   const uint8_t* blk = rp + (c >> 2) * 82u;
   const uint32_t sub = c & 3u;
   const float d = h2f(ld_u16(blk));
-  const uint32_t gl[2] = {ld_u32_a2(blk + 2u + 8u * sub), ld_u32_a2(blk + 6u + 8u * sub)};
-  const uint32_t sg[2] = {ld_u32_a2(blk + 34u + 8u * sub), ld_u32_a2(blk + 38u + 8u * sub)};
+  const uint32_t gl0 = ld_u32_a2(blk + 2u + 8u * sub), gl1 = ld_u32_a2(blk + 6u + 8u * sub);
+  const uint32_t sg0 = ld_u32_a2(blk + 34u + 8u * sub), sg1 = ld_u32_a2(blk + 38u + 8u * sub);
   const uint32_t qh = ld_u16(blk + 66u + 2u * sub);
   const uint32_t sc = ld_u16(blk + 74u + 2u * sub);
-  float res = 0.f;
+  int ha, la, hb, lb;
+  iq2s_sub(gl0, sg0, qh & 0xffu, sc & 0xffu, x.ah, x.al, t, ha, la);
+  iq2s_sub(gl1, sg1, qh >> 8, sc >> 8, x.bh, x.bl, t, hb, lb);
+  // w = d (2 nib + 1) / 8 * v
+  return (d * 0.125f) * (planes_value(ha, la, x.sa) + planes_value(hb, lb, x.sb));
+}
+
+// One IQ3_S sub-block (32 weights: 4 groups of two 4-weight grid entries) against one
+// half of x: integer sums (h, l).
+__device__ __forceinline__ void iq3s_sub(uint32_t q0, uint32_t q1, uint32_t qhb, uint32_t sg,
+                                         const uint32_t* H, const uint32_t* L,
+                                         const IqTables& t, int& h, int& l) {
+  const uint32_t hb0 = spread1x4(qhb & 0x0fu), hb1 = spread1x4(qhb >> 4);
+  uint32_t idx[8];
+  idx[0] = pair_bytes<0>(q0, hb0);
+  idx[1] = pair_bytes<1>(q0, hb0);
+  idx[2] = pair_bytes<2>(q0, hb0);
+  idx[3] = pair_bytes<3>(q0, hb0);
+  idx[4] = pair_bytes<0>(q1, hb1);
+  idx[5] = pair_bytes<1>(q1, hb1);
+  idx[6] = pair_bytes<2>(q1, hb1);
+  idx[7] = pair_bytes<3>(q1, hb1);
+  int ih = 0, il = 0;
 #pragma unroll
-  for (int ib = 0; ib < 2; ++ib) {
-    const uint32_t* H = ib ? x.bh : x.ah;
-    const uint32_t* Lp = ib ? x.bl : x.al;
-    const uint32_t qhb = (qh >> (8 * ib)) & 0xffu;
-    int ih[2] = {0, 0}, il[2] = {0, 0};
-#pragma unroll
-    for (int g = 0; g < 4; ++g) {
-      const uint32_t idx = byte_of(gl[ib], g) | ((qhb << (8 - 2 * g)) & 0x300u);
-      const uint2 k2 = t.kgrid2[idx * kIq2Copies];
-      uint32_t u0, u1;
-      if constexpr (kIq2AluSigns) {
-        // table bytes are 2k ^ 9; a set sign bit flips them with 0x0E (2k ^ 7)
-        const uint32_t sb = byte_of(sg[ib], g);
-        u0 = k2.x ^ (sign_bytes4(sb & 0x0fu) & 0x0e0e0e0eu);
-        u1 = k2.y ^ (sign_bytes4(sb >> 4) & 0x0e0e0e0eu);
-      } else {
-        const uint2 sm = t.sign2[byte_of(sg[ib], g) << 4];
-        u0 = k2.x ^ sm.x ^ 0x09090909u;
-        u1 = k2.y ^ sm.y ^ 0x09090909u;
-      }
-      ih[g >> 1] = dp4a(u1, H[2 * g + 1], dp4a(u0, H[2 * g], ih[g >> 1]));
-      il[g >> 1] = dp4a(u1, Lp[2 * g + 1], dp4a(u0, Lp[2 * g], il[g >> 1]));
+  for (int g = 0; g < 4; ++g) {
+    const uint32_t sb = (sg >> (8 * g)) & 0xffu;
+    uint32_t m0, m1;
+    if constexpr (kIq3TableSigns) {
+      const uint2 sm = t.sign3[sb << 4];
+      m0 = sm.x;
+      m1 = sm.y;
+    } else {
+      m0 = sign_bytes4(sb & 0x0fu) & 0xFEFEFEFEu;
+      m1 = sign_bytes4(sb >> 4) & 0xFEFEFEFEu;
     }
-    const float s = ib ? x.sb : x.sa;
-    const float p0 = planes_value(ih[0] - 8 * x.qh[2 * ib], il[0] - 8 * x.ql[2 * ib], s);
-    const float p1 = planes_value(ih[1] - 8 * x.qh[2 * ib + 1], il[1] - 8 * x.ql[2 * ib + 1], s);
-    const uint32_t sb = (sc >> (8 * ib)) & 0xffu;
-    const float s_lo = d * (0.5f + u2f_small(sb & 0x0fu)) * 0.25f;
-    const float s_hi = d * (0.5f + u2f_small(sb >> 4u)) * 0.25f;
-    res += s_lo * p0 + s_hi * p1;
+    const uint32_t v0 = t.grid3[idx[2 * g] * kIq3Copies] ^ m0;
+    const uint32_t v1 = t.grid3[idx[2 * g + 1] * kIq3Copies] ^ m1;
+    ih = dp4a(v1, H[2 * g + 1], dp4a(v0, H[2 * g], ih));
+    il = dp4a(v1, L[2 * g + 1], dp4a(v0, L[2 * g], il));
   }
-  return res;
+  h = ih;
+  l = il;
 }
 
 template <>
@@ -522,40 +582,19 @@ __device__ __forceinline__ float chunk_dot<QG_FMT_IQ3S>(const uint8_t* rp, const
 #pragma unroll
   for (int i = 0; i < 4; ++i) qs[i] = ld_u32_a2(blk + 2u + 16u * sub + 4u * i);
   const uint32_t qh = ld_u16(blk + 66u + 2u * sub);
-  const uint32_t sg[2] = {ld_u32_a2(blk + 74u + 8u * sub), ld_u32_a2(blk + 78u + 8u * sub)};
+  const uint32_t sg0 = ld_u32_a2(blk + 74u + 8u * sub), sg1 = ld_u32_a2(blk + 78u + 8u * sub);
   const uint32_t sb = blk[106u + sub];
-  float res = 0.f;
-#pragma unroll
-  for (int ib = 0; ib < 2; ++ib) {
-    const uint32_t* H = ib ? x.bh : x.ah;
-    const uint32_t* Lp = ib ? x.bl : x.al;
-    const uint32_t qhb = (qh >> (8 * ib)) & 0xffu;
-    int ih = 0, il = 0;
-#pragma unroll
-    for (int g = 0; g < 4; ++g) {
-      const uint2 sm = t.sign3[byte_of(sg[ib], g) << 4];
-#pragma unroll
-      for (int p = 0; p < 2; ++p) {
-        const int sel = 2 * g + p;
-        const uint32_t qb = byte_of(qs[2 * ib + (sel >> 2)], sel & 3);
-        const uint32_t idx = qb | (((qhb >> sel) & 1u) << 8u);
-        const uint32_t u = t.grid3[idx * kIq3Copies] ^ 0x11111111u ^ (p ? sm.y : sm.x);
-        ih = dp4a(u, H[sel], ih);
-        il = dp4a(u, Lp[sel], il);
-      }
-    }
-    const float s = ib ? x.sb : x.sa;
-    const float pv = planes_value(ih - 15 * (x.qh[2 * ib] + x.qh[2 * ib + 1]),
-                                  il - 15 * (x.ql[2 * ib] + x.ql[2 * ib + 1]), s);
-    const uint32_t nib = ib ? (sb >> 4u) : (sb & 0x0fu);
-    res += d * u2f_small(1u + 2u * nib) * pv;
-  }
-  return res;
+  int ha, la, hb, lb;
+  iq3s_sub(qs[0], qs[1], qh & 0xffu, sg0, x.ah, x.al, t, ha, la);
+  iq3s_sub(qs[2], qs[3], qh >> 8, sg1, x.bh, x.bl, t, hb, lb);
+  // w = d (1 + 2 nib) * v, one scale per 32-weight sub-block (= one half of x)
+  const float s0 = u2f_small(1u + 2u * (sb & 0x0fu)), s1 = u2f_small(1u + 2u * (sb >> 4));
+  return d * (s0 * planes_value(ha, la, x.sa) + s1 * planes_value(hb, lb, x.sb));
 }
 
 // The replicated tables, built at compile time from the codebooks (in the IqTables
-// layout: kIq2TableBytes for IQ2_S, 64 KB for IQ3_S) and copied into each CTA's
-// shared memory with one bulk copy.
+// layout: kIq2TableBytes for IQ2_S, kIq3TableBytes for IQ3_S) and copied into each
+// CTA's shared memory with one bulk copy.
 struct __align__(16) ReplicatedTables {
   uint32_t w[(kIq2TableBytes > kIq3TableBytes ? kIq2TableBytes : kIq3TableBytes) / 4u];
 };
@@ -584,16 +623,15 @@ constexpr ReplicatedTables make_iq2s() {
     const uint32_t G = kIq2Kgrid[e];
     uint32_t lo = 0u, hi = 0u;
     for (uint32_t l = 0; l < 4u; ++l) {
-      lo |= (((G >> (2u * l)) & 3u) << 1) << (8u * l);
-      hi |= (((G >> (2u * (l + 4u))) & 3u) << 1) << (8u * l);
+      lo |= ((((G >> (2u * l)) & 3u) << 1) | 1u) << (8u * l);
+      hi |= ((((G >> (2u * (l + 4u))) & 3u) << 1) | 1u) << (8u * l);
     }
     for (uint32_t r = 0; r < kIq2Copies; ++r) {
       const uint32_t slot = kIq2Copies * e + r;
-      t.w[2u * slot] = kIq2AluSigns ? lo ^ 0x09090909u : lo;
-      t.w[2u * slot + 1u] = kIq2AluSigns ? hi ^ 0x09090909u : hi;
+      t.w[2u * slot] = lo;
+      t.w[2u * slot + 1u] = hi;
     }
   }
-  if (!kIq2AluSigns) put_sign_copies(t, kIq2SignWord, 0x0eu);
   return t;
 }
 
@@ -602,7 +640,7 @@ constexpr ReplicatedTables make_iq3s() {
   for (uint32_t e = 0; e < 512u; ++e) {
     for (uint32_t r = 0; r < kIq3Copies; ++r) t.w[e * kIq3Copies + r] = kIq3Grid[e];
   }
-  put_sign_copies(t, kIq3SignByte / 4u, 0x1eu);
+  if (kIq3TableSigns) put_sign_copies(t, kIq3SignByte / 4u, 0xfeu);
   return t;
 }
 }  // namespace tables_detail
@@ -632,7 +670,6 @@ __device__ __forceinline__ IqTables iq_tables(const uint8_t* base, uint32_t lane
   t.k = lane & 15u;
   if (FMT == QG_FMT_IQ2S) {
     t.kgrid2 = reinterpret_cast<const uint2*>(base) + (t.k & (kIq2Copies - 1u));
-    t.sign2 = reinterpret_cast<const uint2*>(base) + kIq2SignWord / 2u + t.k;
   } else if (FMT == QG_FMT_IQ3S) {
     t.grid3 = reinterpret_cast<const uint32_t*>(base) + (lane & (kIq3Copies - 1u));
     t.sign3 = reinterpret_cast<const uint2*>(base + kIq3SignByte) + t.k;

@@ -9,6 +9,7 @@ be built, `lib()` raises.
 from __future__ import annotations
 
 import ctypes
+import os
 import re
 from ctypes import c_float, c_int, c_uint32, c_uint64, c_void_p
 from pathlib import Path
@@ -97,9 +98,13 @@ def header_functions(header: Path = HEADER) -> list[str]:
 
 
 def lib() -> ctypes.CDLL:
+    """The library: the in-tree build (rebuilt when a source is newer), or the build
+    named by QG_LIBRARY (another build of the same sources, e.g. with different tuning
+    macros, for side-by-side measurements)."""
     global _LIB
     if _LIB is None:
-        path = _build.build()
+        override = os.environ.get("QG_LIBRARY")
+        path = Path(override) if override else _build.build()
         handle = ctypes.CDLL(str(path))
         for name, argtypes in SIGNATURES.items():
             fn = getattr(handle, name)
