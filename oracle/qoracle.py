@@ -122,6 +122,8 @@ class Ref:
         L.ref_argmax.restype = c_uint32
         L.ref_apply_kv.argtypes = [c_void_p, c_uint32, c_void_p, c_uint64, c_uint32, c_uint32, c_uint32]
         L.ref_feedback.argtypes = [c_int, c_void_p, c_uint32, c_void_p, c_uint32, c_void_p, c_uint32, c_float, c_int]
+        L.ref_cache_gated_product.argtypes = [c_void_p, c_uint32, c_void_p, c_uint32, c_void_p, c_uint32,
+                                              c_void_p, c_uint32, c_float, c_int]
         L.ref_time_stage_logits.argtypes = [c_int, c_void_p, c_void_p, c_void_p, c_uint32, c_uint32, c_uint32, c_void_p]
         L.ref_time_stage_logits.restype = c_double
 
@@ -157,6 +159,11 @@ class Ref:
         logits = np.ascontiguousarray(logits, np.float32)
         self.lib.ref_feedback(kind, _p(logits), logits.size, _p(act), act.size,
                               _p(cache), 0 if cache is None else cache.size, eps, accumulate)
+
+    def cache_gated_product(self, logits, gate, up, act, eps, accumulate) -> None:
+        logits = np.ascontiguousarray(logits, np.float32)
+        self.lib.ref_cache_gated_product(_p(logits), logits.size, _p(gate), gate.size, _p(up), up.size,
+                                         _p(act), act.size, eps, accumulate)
 
     def time_matvec(self, fmt, payload, meta, x, rows, cols, threads) -> tuple[float, np.ndarray]:
         y = np.empty(rows, np.float32)

@@ -192,6 +192,23 @@ void ref_feedback(int kind, const float* logits, std::uint32_t rows, float* act,
   }
 }
 
+// The CPU twin of rmsnorm_cache_and_gated_product (decode_kernels.cu:263-289) as the
+// mixed runner's CPU reference applies it (main.cpp:2620-2633): the up cache gets the
+// normalised logits (accumulated or not), then activation = gate cache x up cache
+// (main.cpp:1459-1503).
+void ref_cache_gated_product(const float* logits, std::uint32_t rows, const float* gate,
+                             std::uint32_t gate_cols, float* up, std::uint32_t up_cols,
+                             float* act, std::uint32_t cols, float eps, int accumulate) {
+  const std::vector<float> lg(logits, logits + rows);
+  const std::vector<float> g(gate, gate + gate_cols);
+  std::vector<float> u(up, up + up_cols);
+  std::vector<float> a(act, act + cols);
+  apply_reference_rmsnorm_cache(lg, u, cols, eps, false, accumulate != 0);
+  apply_reference_gated_cache_product(g, u, a, cols);
+  std::memcpy(up, u.data(), std::min<std::size_t>(u.size(), up_cols) * sizeof(float));
+  std::memcpy(act, a.data(), cols * sizeof(float));
+}
+
 // CPU baseline: time reference_stage_logits over rows [0, rows) split into
 // `threads` contiguous row slices, one std::thread each (the reference function
 // itself is single-threaded).  Payload slices are gathered before the clock

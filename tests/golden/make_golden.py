@@ -145,6 +145,19 @@ def main(argv: list[str]) -> int:
                 key = f"k{kind}_e{int(round(-np.log10(eps)))}_a{acc}"
                 arrays.update({f"{key}_act_in": act, f"{key}_cache_in": cache,
                                f"{key}_act": a2, f"{key}_cache": c2})
+    # rmsnorm_cache_and_gated_product: the up cache takes the normalised logits (overwritten
+    # or accumulated), the activation is gate x up (decode_kernels.cu:263-289 as the mixed
+    # runner's CPU reference applies it).
+    for eps in (1e-6, 1e-5):
+        for acc in (0, 1):
+            gate = rng.standard_normal(96).astype(np.float32)
+            up = rng.standard_normal(96).astype(np.float32)
+            act = rng.standard_normal(96).astype(np.float32)
+            u2, a2 = up.copy(), act.copy()
+            ref.cache_gated_product(logits, gate, u2, a2, eps, acc)
+            key = f"k6_e{int(round(-np.log10(eps)))}_a{acc}"
+            arrays.update({f"{key}_gate": gate, f"{key}_up_in": up, f"{key}_act_in": act,
+                           f"{key}_up": u2, f"{key}_act": a2})
     np.savez_compressed(OUT / "golden_feedback.npz", **arrays)
     print("done")
     return 0

@@ -264,6 +264,40 @@ def test_feedback_launchers_vs_golden(cuda):
                 np.testing.assert_allclose(cache.cpu().numpy()[: want_cache.size], want_cache, rtol=2e-6, atol=2e-6)
 
 
+def test_gated_product_launcher_vs_golden(cuda):
+    """rtxllm_launch_rmsnorm_cache_and_gated_product (decode_kernels.cu:263-289; the mixed
+    runner's finalising FFN edge, main.cpp:4113) against the reference's CPU twin: up cache
+    overwritten or accumulated, activation = gate x up."""
+    import qgemv_b200
+    from conftest import GOLDEN
+
+    g = np.load(GOLDEN / "golden_feedback.npz")
+    logits = dev(g["logits"], cuda)
+    n = g["logits"].size
+    s = torch.cuda.current_stream().cuda_stream
+    for eps_tag, eps in (("e6", 1e-6), ("e5", 1e-5)):
+        for acc in (0, 1):
+            key = f"k6_{eps_tag}_a{acc}"
+            gate, up, act = dev(g[f"{key}_gate"], cuda), dev(g[f"{key}_up_in"], cuda), dev(g[f"{key}_act_in"], cuda)
+            cols = act.numel()
+            code = qgemv_b200.call("rtxllm_launch_rmsnorm_cache_and_gated_product", logits.data_ptr(),
+                                   gate.data_ptr(), up.data_ptr(), act.data_ptr(), n, up.numel(), cols,
+                                   eps, acc, s)
+            assert code == 0
+            np.testing.assert_allclose(up.cpu().numpy(), g[f"{key}_up"], rtol=2e-6, atol=2e-6, err_msg=key)
+            np.testing.assert_allclose(act.cpu().numpy(), g[f"{key}_act"], rtol=2e-6, atol=2e-6, err_msg=key)
+    # validation as decode_kernels.cu:3227-3229: zero cache or output columns are
+    # cudaErrorInvalidValue; zero rows launch a kernel that returns at once (nothing written)
+    up0 = torch.ones(4, device=cuda)
+    call = lambda rows, cc, oc: qgemv_b200.call(  # noqa: E731
+        "rtxllm_launch_rmsnorm_cache_and_gated_product", logits.data_ptr(), up0.data_ptr(),
+        up0.data_ptr(), up0.data_ptr(), rows, cc, oc, 1e-6, 0, s)
+    assert call(n, 0, 4) == 1 and call(n, 4, 0) == 1
+    assert call(0, 4, 4) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(up0, torch.ones(4, device=cuda))
+
+
 def test_batched_vs_oracle(cuda, port):
     for fmt in (packs.Q4K_RAW, packs.IQ2S):
         rows, cols, batch = 96, 2048, 5

@@ -132,6 +132,23 @@ def test_feedback_port_matches_reference():
                                                g[f"{key}_cache"][:cols], rtol=1e-6, atol=1e-6)
 
 
+def test_gated_product_port_matches_reference():
+    """rmsnorm_cache_and_gated_product (decode_kernels.cu:263-289): the C restatement
+    against the reference's own CPU twin (golden vectors)."""
+    import qoracle
+
+    g = np.load(GOLDEN / "golden_feedback.npz")
+    L = qoracle.Port().lib
+    logits = g["logits"]
+    for eps_tag, eps in (("e6", 1e-6), ("e5", 1e-5)):
+        for acc in (0, 1):
+            key = f"k6_{eps_tag}_a{acc}"
+            gate, up, act = g[f"{key}_gate"], g[f"{key}_up_in"].copy(), g[f"{key}_act_in"].copy()
+            L.orc_rmsnorm_cache_and_gated_product(logits.ctypes.data, gate.ctypes.data, up.ctypes.data,
+                                                  act.ctypes.data, logits.size, up.size, act.size, eps, acc)
+            assert same_bits(up, g[f"{key}_up"]) and same_bits(act, g[f"{key}_act"]), key
+
+
 def test_planted_mistake_is_caught(port):
     """A corrupted payload byte must break bit-exactness and the logit tolerance."""
     g = load_golden(packs.Q4K_RAW, "small")
