@@ -89,7 +89,9 @@ static inline uint32_t qg_meta_bytes_per_block(int fmt) {
 }
 
 /* Error word bits (set by kernels, read and cleared by qg_get_error). */
-#define QG_ERR_WAIT_TIMEOUT 0x1u /* a bounded wait on a TMA barrier ran out */
+#define QG_ERR_WAIT_TIMEOUT 0x1u /* a bounded wait (TMA barrier, exchange word) ran out */
+#define QG_ERR_POSITION 0x2u     /* a decode position read from device memory was past the
+                                    KV cache or the step graph's context bucket */
 
 /* ===========================================================================
  * 1. Drop-in launchers (reference: runtime/kernels/decode/decode_kernels.h)
@@ -356,19 +358,24 @@ cudaError_t qg_graph_destroy(qg_graph graph);
  * attention over positions [0, pos] -> Wo -> all-reduce (+x) -> rmsnorm -> gate,up ->
  * silu(g)*u -> Wd -> all-reduce (+x1); then final rmsnorm, vocab head and the global
  * argmax (lowest index wins ties) into *token.  head_dim must be 128 and
- * n_q_heads / n_kv_heads one of 1, 2, 4, 8, 16.  With
- * collective = 0 the all-reduces are fused into the Wo/Wd GEMVs and the following
- * RMSNorm over NVLink peer memory (qg_decoder_create allocates and maps the exchange
- * buffers, up to 8 ranks).  All launches and NCCL collectives go on the caller's stream
- * (graph-capturable).
+ * n_q_heads / n_kv_heads one of 1, 2, 4, 8, 16.  Every tensor-parallel degree computes
+ * the single-GPU step bit for bit (hidden state and token): the row-parallel Wo / Wd sums
+ * follow one canonical order -- the row cut into up to 8 column segments (the shards at
+ * the largest degree), each summed in a fixed order, the segments in a pairwise tree,
+ * the ranks added in the same tree, then the residual -- and every RMSNorm uses one fixed
+ * sum-of-squares order.  With collective = 0 the all-reduces are fused into the Wo/Wd
+ * GEMVs and the following RMSNorm over NVLink peer memory (up to 8 ranks); with
+ * collective = 1 the same exchange words travel through ncclAllGather between the
+ * kernels (same bits, the baseline).  All launches and NCCL collectives go on the
+ * caller's stream (graph-capturable).
  * ------------------------------------------------------------------------- */
 typedef struct qg_decoder_dims {
   uint32_t layers, hidden, n_q_heads, n_kv_heads, head_dim, ffn, vocab, ctx_max;
   float eps, rope_base;
   int attn_fmt, ffn_fmt, down_fmt, head_fmt;
   uint32_t tp_rank, tp_size;
-  uint32_t collective;  /* tp_size > 1: 0 = all-reduces fused into the GEMVs over NVLink peer
-                           memory (CUDA IPC), 1 = ncclAllReduce between the kernels */
+  uint32_t collective;  /* tp_size > 1: 0 = exchanges fused into the GEMVs over NVLink peer
+                           memory (CUDA IPC), 1 = the same words moved by ncclAllGather */
 } qg_decoder_dims;
 
 typedef struct qg_decoder_layer {
@@ -387,13 +394,36 @@ cudaError_t qg_nccl_unique_id(void* id_out);
 cudaError_t qg_decoder_workspace_bytes(const qg_decoder_dims* d, size_t* bytes);
 cudaError_t qg_decoder_shard(const qg_decoder_dims* d, uint32_t* q_rows, uint32_t* kv_rows,
                              uint32_t* ffn_rows, uint32_t* vocab_rows, uint32_t* vocab_offset);
-/* Collective over the tp_size ranks when tp_size > 1 (NCCL communicator setup). */
+/* Bytes of a rank's exchange region (0 for tp_size 1). */
+cudaError_t qg_decoder_exchange_bytes(const qg_decoder_dims* d, size_t* bytes);
+/* Collective over the tp_size ranks when tp_size > 1 (NCCL communicator setup).  The
+ * exchange region is allocated with cudaMalloc and shared through CUDA IPC. */
 cudaError_t qg_decoder_create(const qg_decoder_dims* d, const qg_decoder_layer* layers,
                               const float* final_norm, const uint8_t* head,
                               const uint8_t* head_meta, void* workspace, const void* nccl_id,
                               qg_decoder* out);
+/* The same with a caller-owned exchange region (tp_size > 1): 256-B aligned,
+ * qg_decoder_exchange_bytes long, inside device memory from cudaMalloc (for example an
+ * arena of the reference's VramSuperallocator, runtime/core/allocator/vram_superallocator.h:36-44),
+ * whose allocation the peers map through CUDA IPC at the region's offset.  The library
+ * allocates no device memory itself (NCCL's communicator aside). */
+cudaError_t qg_decoder_create_in(const qg_decoder_dims* d, const qg_decoder_layer* layers,
+                                 const float* final_norm, const uint8_t* head,
+                                 const uint8_t* head_meta, void* workspace, void* exchange,
+                                 const void* nccl_id, qg_decoder* out);
+/* One decode step at position `pos` (0 <= pos < ctx_max), baked into the launches. */
 cudaError_t qg_decoder_step(qg_decoder dec, const float* x, uint32_t pos, uint32_t* token,
                             cudaStream_t stream);
+/* One decode step whose position is read on the device: *pos_dev (RoPE angle and cache
+ * slot), attention over [0, *pos_dev] with its grid sized for ctx_bucket positions
+ * (1 <= ctx_bucket <= ctx_max); advance != 0 adds 1 to *pos_dev after the token is
+ * chosen.  One graph captured per context bucket then serves every token whose position
+ * is below the bucket (the "one captured graph per decode step and bucket" of the
+ * reference's graph runner, runtime/core/graphs/cuda_graph_bucket.h:70-139).  A position
+ * at or past the bucket writes nothing to the caches and sets QG_ERR_POSITION. */
+cudaError_t qg_decoder_step_at(qg_decoder dec, const float* x, uint32_t* pos_dev,
+                               uint32_t ctx_bucket, uint32_t advance, uint32_t* token,
+                               cudaStream_t stream);
 /* Device pointers of the last step's final hidden state and this rank's logits. */
 cudaError_t qg_decoder_views(qg_decoder dec, float** hidden, float** logits);
 cudaError_t qg_decoder_destroy(qg_decoder dec);

@@ -20,15 +20,29 @@
 
 namespace qg {
 
+extern __device__ unsigned int g_error_word;
+
 constexpr uint32_t kHeadDim = 128;
 constexpr uint32_t kSpan = 64;       // positions per attention CTA
 constexpr uint32_t kMaxGroup = 16;   // q heads per kv head
 
+// The token position: `pos`, or *pos_dev when the step reads it from device memory
+// (graphs replayed for successive tokens).
+__device__ __forceinline__ uint32_t step_position(uint32_t pos, const uint32_t* pos_dev) {
+  return pos_dev != nullptr ? *reinterpret_cast<const volatile uint32_t*>(pos_dev) : pos;
+}
+
 __global__ void rope_append_kernel(float* q, float* k, const float* v, __half* k_cache,
                                    __half* v_cache, uint32_t n_q, uint32_t n_kv, uint32_t ctx_max,
-                                   uint32_t pos, float rope_base) {
+                                   uint32_t pos_arg, const uint32_t* pos_dev, uint32_t ctx_limit,
+                                   float rope_base) {
   pdl_wait();
   pdl_trigger();
+  const uint32_t pos = step_position(pos_arg, pos_dev);
+  if (pos >= ctx_limit) {  // a position past the cache (or the graph's bucket): no write
+    if (blockIdx.x == 0u && threadIdx.x == 0u) atomicOr(&g_error_word, QG_ERR_POSITION);
+    return;
+  }
   // one thread per rotation pair of one head (q heads first, then k heads), plus the
   // v copy done by the k-head threads
   const uint32_t pairs = kHeadDim / 2u;
@@ -55,11 +69,12 @@ __global__ void rope_append_kernel(float* q, float* k, const float* v, __half* k
 
 cudaError_t launch_rope_append(float* q, float* k, const float* v, void* k_cache, void* v_cache,
                                uint32_t n_q, uint32_t n_kv, uint32_t ctx_max, uint32_t pos,
-                               float rope_base, cudaStream_t stream) {
+                               const uint32_t* pos_dev, uint32_t ctx_limit, float rope_base,
+                               cudaStream_t stream) {
   const uint32_t threads = (n_q + n_kv) * (kHeadDim / 2u);
   return launch_k(rope_append_kernel, (threads + 127u) / 128u, 128, 0, stream, q, k, v,
                   static_cast<__half*>(k_cache), static_cast<__half*>(v_cache), n_q, n_kv, ctx_max,
-                  pos, rope_base);
+                  pos, pos_dev, ctx_limit < ctx_max ? ctx_limit : ctx_max, rope_base);
 }
 
 // Partial attention of one kv head over positions [span*kSpan, min(+kSpan, ctx_len)),
@@ -72,7 +87,8 @@ template <uint32_t G>
 __global__ void __launch_bounds__(128) attn_split_kernel(const float* __restrict__ q,
                                                          const __half* __restrict__ k_cache,
                                                          const __half* __restrict__ v_cache,
-                                                         uint32_t ctx_max, uint32_t ctx_len,
+                                                         uint32_t ctx_max, uint32_t ctx_len_arg,
+                                                         const uint32_t* pos_dev, uint32_t ctx_limit,
                                                          uint32_t spans, float* partial) {
   static_assert(kSpan * 2u == 128u, "two threads per position");
   __shared__ __align__(16) float qs[G][kHeadDim];
@@ -82,10 +98,12 @@ __global__ void __launch_bounds__(128) attn_split_kernel(const float* __restrict
   const uint32_t kv = blockIdx.x, span = blockIdx.y, tid = threadIdx.x;
   const uint32_t lane = tid & 31u, warp = tid >> 5;
   const uint32_t t0 = span * kSpan;
-  const uint32_t n = ctx_len > t0 ? min(kSpan, ctx_len - t0) : 0u;
   const float scale = rsqrtf(static_cast<float>(kHeadDim));
   pdl_wait();
   pdl_trigger();
+  const uint32_t ctx_len = pos_dev != nullptr ? min(step_position(0u, pos_dev) + 1u, ctx_limit) : ctx_len_arg;
+  if (t0 >= ctx_len) return;  // a span of the graph's bucket beyond this token's context
+  const uint32_t n = min(kSpan, ctx_len - t0);
   for (uint32_t i = tid; i < G * kHeadDim; i += blockDim.x) {
     qs[i / kHeadDim][i % kHeadDim] = q[(kv * G) * kHeadDim + i] * scale;
   }
@@ -236,7 +254,9 @@ __global__ void __launch_bounds__(128) attn_split_tc_kernel(const float* __restr
                                                             const __half* __restrict__ k_cache,
                                                             const __half* __restrict__ v_cache,
                                                             uint32_t G, uint32_t ctx_max,
-                                                            uint32_t ctx_len, uint32_t spans,
+                                                            uint32_t ctx_len_arg,
+                                                            const uint32_t* pos_dev,
+                                                            uint32_t ctx_limit, uint32_t spans,
                                                             float* partial) {
   static_assert(kSpan == 64u, "four warps of 16 positions");
   __shared__ __align__(128) uint8_t vs[kSpan * kHeadDim * 2u];  // the span's V, swizzled
@@ -246,10 +266,12 @@ __global__ void __launch_bounds__(128) attn_split_tc_kernel(const float* __restr
   const uint32_t kv = blockIdx.x, span = blockIdx.y, tid = threadIdx.x;
   const uint32_t lane = tid & 31u, warp = tid >> 5, g = lane >> 2, t = lane & 3u;
   const uint32_t t0 = span * kSpan;
-  const uint32_t n = ctx_len > t0 ? min(kSpan, ctx_len - t0) : 0u;
   const float scale = rsqrtf(static_cast<float>(kHeadDim));
   pdl_wait();  // q and the newest K/V row come from the previous kernel
   pdl_trigger();
+  const uint32_t ctx_len = pos_dev != nullptr ? min(step_position(0u, pos_dev) + 1u, ctx_limit) : ctx_len_arg;
+  if (t0 >= ctx_len) return;  // a span of the graph's bucket beyond this token's context
+  const uint32_t n = min(kSpan, ctx_len - t0);
 
   // V of the span -> shared memory (rows past the context are zero).
   const __half* vbase = v_cache + (static_cast<size_t>(kv) * ctx_max + t0) * kHeadDim;
@@ -374,12 +396,15 @@ __global__ void __launch_bounds__(128) attn_split_tc_kernel(const float* __restr
 constexpr uint32_t kMaxSpans = 4096;
 
 __global__ void __launch_bounds__(64) attn_combine_kernel(const float* __restrict__ partial,
-                                                          uint32_t spans, uint32_t used_spans,
+                                                          uint32_t spans, uint32_t used_arg,
+                                                          const uint32_t* pos_dev, uint32_t ctx_limit,
                                                           float* out, ActChunk* act) {
   __shared__ float wgt[kMaxSpans];
   __shared__ float red[2];
   pdl_wait();
   pdl_trigger();
+  const uint32_t used_spans =
+      pos_dev != nullptr ? (min(step_position(0u, pos_dev) + 1u, ctx_limit) + kSpan - 1u) / kSpan : used_arg;
   const uint32_t h = blockIdx.x, tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
   const uint32_t stride = kHeadDim + 2u;
   const float* base = partial + static_cast<size_t>(h) * spans * stride;
@@ -433,9 +458,13 @@ cudaError_t attn_partial_floats(uint32_t n_q, uint32_t ctx_max, size_t* floats) 
   return cudaSuccess;
 }
 
+// ctx_len: positions [0, ctx_len) when pos_dev is null; otherwise the context is
+// [0, *pos_dev] and ctx_len is the bucket the grid is sized for (positions past it are
+// not read).
 cudaError_t launch_attention(const float* q, const void* k_cache, const void* v_cache,
                              uint32_t n_q, uint32_t n_kv, uint32_t ctx_max, uint32_t ctx_len,
-                             float* partial, float* out, void* act, cudaStream_t stream) {
+                             const uint32_t* pos_dev, float* partial, float* out, void* act,
+                             cudaStream_t stream) {
   if (n_kv == 0u || n_q % n_kv != 0u || n_q / n_kv > kMaxGroup || ctx_len == 0u ||
       ctx_len > ctx_max || (ctx_max + kSpan - 1u) / kSpan > kMaxSpans) {
     return cudaErrorInvalidValue;
@@ -452,22 +481,28 @@ cudaError_t launch_attention(const float* q, const void* k_cache, const void* v_
                   (reinterpret_cast<uintptr_t>(vc) & 15u) == 0u;
   if (tc) {
     e = launch_k(attn_split_tc_kernel, grid, 128, 0, stream, q, kc, vc, group, ctx_max, ctx_len,
-                 spans, partial);
+                 pos_dev, ctx_len, spans, partial);
     if (e != cudaSuccess) return e;
     return launch_k(attn_combine_kernel, n_q, 64, 0, stream, static_cast<const float*>(partial),
-                    spans, used, out, static_cast<ActChunk*>(act));
+                    spans, used, pos_dev, ctx_len, out, static_cast<ActChunk*>(act));
   }
   switch (group) {
-    case 1: e = launch_k(attn_split_kernel<1>, grid, 128, 0, stream, q, kc, vc, ctx_max, ctx_len, spans, partial); break;
-    case 2: e = launch_k(attn_split_kernel<2>, grid, 128, 0, stream, q, kc, vc, ctx_max, ctx_len, spans, partial); break;
-    case 4: e = launch_k(attn_split_kernel<4>, grid, 128, 0, stream, q, kc, vc, ctx_max, ctx_len, spans, partial); break;
-    case 8: e = launch_k(attn_split_kernel<8>, grid, 128, 0, stream, q, kc, vc, ctx_max, ctx_len, spans, partial); break;
-    case 16: e = launch_k(attn_split_kernel<16>, grid, 128, 0, stream, q, kc, vc, ctx_max, ctx_len, spans, partial); break;
+#define QG_SPLIT(G)                                                                          \
+  case G:                                                                                    \
+    e = launch_k(attn_split_kernel<G>, grid, 128, 0, stream, q, kc, vc, ctx_max, ctx_len,    \
+                 pos_dev, ctx_len, spans, partial);                                          \
+    break;
+    QG_SPLIT(1)
+    QG_SPLIT(2)
+    QG_SPLIT(4)
+    QG_SPLIT(8)
+    QG_SPLIT(16)
+#undef QG_SPLIT
     default: return cudaErrorInvalidValue;
   }
   if (e != cudaSuccess) return e;
   return launch_k(attn_combine_kernel, n_q, 64, 0, stream, static_cast<const float*>(partial), spans,
-                  used, out, static_cast<ActChunk*>(act));
+                  used, pos_dev, ctx_len, out, static_cast<ActChunk*>(act));
 }
 
 // Local argmax of this rank's vocab shard -> (value bits, global index); lowest index
@@ -524,10 +559,13 @@ __global__ void __launch_bounds__(1024) argmax_candidate_kernel(const float* __r
 }
 
 // token = global argmax over the gathered (value, index) candidates of all ranks.
-__global__ void select_token_kernel(const uint32_t* cand, uint32_t ranks, uint32_t* token) {
+// advance (optional): the step's position counter, incremented once the token is chosen.
+__global__ void select_token_kernel(const uint32_t* cand, uint32_t ranks, uint32_t* token,
+                                    uint32_t* advance) {
   pdl_wait();
   pdl_trigger();
   if (threadIdx.x != 0u || blockIdx.x != 0u) return;
+  if (advance != nullptr) *advance += 1u;
   float bv = __uint_as_float(cand[0]);
   uint32_t bi = cand[1];
   for (uint32_t r = 1; r < ranks; ++r) {
@@ -562,8 +600,8 @@ cudaError_t launch_argmax_candidate(const float* v, uint32_t n, uint32_t offset,
 }
 
 cudaError_t launch_select_token(const uint32_t* cand, uint32_t ranks, uint32_t* token,
-                                cudaStream_t stream) {
-  return launch_k(select_token_kernel, 1, 32, 0, stream, cand, ranks, token);
+                                uint32_t* advance, cudaStream_t stream) {
+  return launch_k(select_token_kernel, 1, 32, 0, stream, cand, ranks, token, advance);
 }
 
 }  // namespace qg

@@ -43,14 +43,16 @@ namespace qg {
 cudaError_t attn_partial_floats(uint32_t n_q, uint32_t ctx_max, size_t* floats);
 cudaError_t launch_rope_append(float* q, float* k, const float* v, void* k_cache, void* v_cache,
                                uint32_t n_q, uint32_t n_kv, uint32_t ctx_max, uint32_t pos,
-                               float rope_base, cudaStream_t stream);
+                               const uint32_t* pos_dev, uint32_t ctx_limit, float rope_base,
+                               cudaStream_t stream);
 cudaError_t launch_attention(const float* q, const void* k_cache, const void* v_cache,
                              uint32_t n_q, uint32_t n_kv, uint32_t ctx_max, uint32_t ctx_len,
-                             float* partial, float* out, void* act, cudaStream_t stream);
+                             const uint32_t* pos_dev, float* partial, float* out, void* act,
+                             cudaStream_t stream);
 cudaError_t launch_argmax_candidate(const float* v, uint32_t n, uint32_t offset, uint32_t* cand,
                                     cudaStream_t stream);
 cudaError_t launch_select_token(const uint32_t* cand, uint32_t ranks, uint32_t* token,
-                                cudaStream_t stream);
+                                uint32_t* advance, cudaStream_t stream);
 }  // namespace qg
 
 namespace {
@@ -154,10 +156,14 @@ cudaError_t nccl_status(ncclResult_t r) {
 
 }  // namespace
 
-// Exchange region of one rank (cudaMalloc, shared through CUDA IPC): the local epoch,
+// Exchange region of one rank (shared with the peers through CUDA IPC): the local epoch,
 // then [2 parities][ranks][hidden] 64-bit words (epoch << 32 | value bits).
 constexpr size_t kExHeader = 256;
 constexpr size_t kExEpoch = 0;  // byte offset inside the header
+
+size_t exchange_bytes(const qg_decoder_dims& d) {
+  return align_up(kExHeader + 2ull * d.tp_size * d.hidden * sizeof(uint64_t));
+}
 
 struct qg_decoder_s {
   qg_decoder_dims dims{};
@@ -171,68 +177,104 @@ struct qg_decoder_s {
   ncclComm_t comm = nullptr;
   uint32_t last_output = 0;  // workspace offset of the last step's final hidden state
   uint8_t* ex_local = nullptr;                   // this rank's exchange region
+  bool ex_owned = false;                         // allocated here (else caller-owned)
   uint8_t* ex_peer[qg::kMaxExchangeRanks] = {};  // every rank's region (self included)
+  void* ex_mapped[qg::kMaxExchangeRanks] = {};   // peers' allocations mapped through IPC
   qg::GemvCanon canon_o{}, canon_d{};            // canonical segments of Wo / Wd on this rank
   bool broken = false;                           // a step failed after enqueueing work
 };
 
 namespace {
 
-// Allocates this rank's exchange region, gathers every rank's IPC handle through NCCL
-// and maps the peers' regions.  The handle all-gather also orders every rank's zeroing
-// of its region before any peer can write into it.
-cudaError_t exchange_setup(qg_decoder_s* dec) {
-  const uint32_t n = dec->dims.tp_size, r = dec->dims.tp_rank;
-  const size_t bytes = kExHeader + 2ull * n * dec->dims.hidden * sizeof(uint64_t);
-  cudaError_t e = cudaMalloc(&dec->ex_local, bytes);
-  if (e != cudaSuccess) return e;
-  e = cudaMemset(dec->ex_local, 0, bytes);
-  if (e != cudaSuccess) return e;
-  if (dec->dims.collective != 0u) {  // NCCL moves the words: the local region only
-    e = cudaDeviceSynchronize();
-    dec->ex_peer[r] = dec->ex_local;
-    return e;
+// Base of the device allocation holding `p` (cuMemGetAddressRange through the runtime's
+// driver entry point: the library does not link libcuda itself).
+cudaError_t allocation_base(void* p, uint8_t** base) {
+  using GetRangeFn = int (*)(unsigned long long* base, size_t* size, unsigned long long ptr);
+  static GetRangeFn fn = nullptr;
+  if (fn == nullptr) {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    const cudaError_t e = cudaGetDriverEntryPoint("cuMemGetAddressRange", &f, cudaEnableDefault, &q);
+    if (e != cudaSuccess) return e;
+    if (q != cudaDriverEntryPointSuccess || f == nullptr) return cudaErrorNotSupported;
+    fn = reinterpret_cast<GetRangeFn>(f);
   }
-  cudaIpcMemHandle_t mine;
-  e = cudaIpcGetMemHandle(&mine, dec->ex_local);
+  unsigned long long b = 0;
+  size_t size = 0;
+  if (fn(&b, &size, reinterpret_cast<unsigned long long>(p)) != 0) return cudaErrorInvalidDevicePointer;
+  *base = reinterpret_cast<uint8_t*>(b);
+  return cudaSuccess;
+}
+
+// One rank's record in the IPC all-gather: the handle of the allocation holding its
+// exchange region and the region's offset in it.
+struct ExchangeRecord {
+  cudaIpcMemHandle_t handle;
+  uint64_t offset;
+  uint8_t pad[128 - sizeof(cudaIpcMemHandle_t) - sizeof(uint64_t)];
+};
+static_assert(sizeof(ExchangeRecord) == 128, "128-byte records");
+
+// Sets up this rank's exchange region -- `region` (caller-owned, exchange_bytes long) or
+// one allocated here -- zeroes it, gathers every rank's IPC record through NCCL (staged in
+// the decoder workspace, which no step uses yet) and maps the peers' regions.  The
+// all-gather also orders every rank's zeroing of its region before any peer can write
+// into it.
+cudaError_t exchange_setup(qg_decoder_s* dec, void* region) {
+  const uint32_t n = dec->dims.tp_size, r = dec->dims.tp_rank;
+  const size_t bytes = exchange_bytes(dec->dims);
+  cudaError_t e = cudaSuccess;
+  if (region != nullptr) {
+    dec->ex_local = static_cast<uint8_t*>(region);
+  } else {
+    e = cudaMalloc(&dec->ex_local, bytes);
+    if (e != cudaSuccess) return e;
+    dec->ex_owned = true;
+  }
+  e = cudaMemset(dec->ex_local, 0, bytes);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
   if (e != cudaSuccess) return e;
-  uint8_t* handles = nullptr;
-  e = cudaMalloc(&handles, n * sizeof(cudaIpcMemHandle_t));
+  dec->ex_peer[r] = dec->ex_local;
+  if (dec->dims.collective != 0u) return cudaSuccess;  // NCCL moves the words: local only
+  uint8_t* base = nullptr;
+  e = allocation_base(dec->ex_local, &base);
   if (e != cudaSuccess) return e;
-  std::vector<cudaIpcMemHandle_t> all(n);
-  e = cudaMemcpy(handles + r * sizeof(mine), &mine, sizeof(mine), cudaMemcpyHostToDevice);
+  ExchangeRecord mine{};
+  e = cudaIpcGetMemHandle(&mine.handle, base);
+  if (e != cudaSuccess) return e;
+  mine.offset = static_cast<uint64_t>(dec->ex_local - base);
+  uint8_t* stage = dec->ws;  // n * 128 bytes of the workspace
+  std::vector<ExchangeRecord> all(n);
+  e = cudaMemcpy(stage + r * sizeof(mine), &mine, sizeof(mine), cudaMemcpyHostToDevice);
   if (e == cudaSuccess) {
-    e = nccl_status(ncclAllGather(handles + r * sizeof(mine), handles, sizeof(mine), ncclUint8,
-                                  dec->comm, nullptr));
+    e = nccl_status(ncclAllGather(stage + r * sizeof(mine), stage, sizeof(mine), ncclUint8, dec->comm,
+                                  nullptr));
   }
   if (e == cudaSuccess) e = cudaStreamSynchronize(nullptr);
   if (e == cudaSuccess) {
-    e = cudaMemcpy(all.data(), handles, n * sizeof(cudaIpcMemHandle_t), cudaMemcpyDeviceToHost);
+    e = cudaMemcpy(all.data(), stage, n * sizeof(ExchangeRecord), cudaMemcpyDeviceToHost);
   }
-  cudaFree(handles);
   if (e != cudaSuccess) return e;
   for (uint32_t p = 0; p < n; ++p) {
-    if (p == r) {
-      dec->ex_peer[p] = dec->ex_local;
-      continue;
-    }
+    if (p == r) continue;
     void* ptr = nullptr;
-    e = cudaIpcOpenMemHandle(&ptr, all[p], cudaIpcMemLazyEnablePeerAccess);
+    e = cudaIpcOpenMemHandle(&ptr, all[p].handle, cudaIpcMemLazyEnablePeerAccess);
     if (e != cudaSuccess) return e;
-    dec->ex_peer[p] = static_cast<uint8_t*>(ptr);
+    dec->ex_mapped[p] = ptr;
+    dec->ex_peer[p] = static_cast<uint8_t*>(ptr) + all[p].offset;
   }
   return cudaSuccess;
 }
 
 void exchange_teardown(qg_decoder_s* dec) {
   for (uint32_t p = 0; p < qg::kMaxExchangeRanks; ++p) {
-    if (dec->ex_peer[p] != nullptr && dec->ex_peer[p] != dec->ex_local) {
-      cudaIpcCloseMemHandle(dec->ex_peer[p]);
-    }
+    if (dec->ex_mapped[p] != nullptr) cudaIpcCloseMemHandle(dec->ex_mapped[p]);
+    dec->ex_mapped[p] = nullptr;
     dec->ex_peer[p] = nullptr;
   }
-  if (dec->ex_local != nullptr) cudaFree(dec->ex_local);
+  if (dec->ex_owned && dec->ex_local != nullptr) cudaFree(dec->ex_local);
   dec->ex_local = nullptr;
+  dec->ex_owned = false;
 }
 
 // The Wo / Wd GEMV side of an exchange: this rank's slot in every rank's region (fused
@@ -281,13 +323,16 @@ cudaError_t qg_decoder_shard(const qg_decoder_dims* d, uint32_t* q_rows, uint32_
   return cudaSuccess;
 }
 
-cudaError_t qg_decoder_create(const qg_decoder_dims* d, const qg_decoder_layer* layers,
-                              const float* final_norm, const uint8_t* head,
-                              const uint8_t* head_meta, void* workspace, const void* nccl_id,
-                              qg_decoder* out) {
+}  // extern "C"
+
+namespace {
+
+cudaError_t decoder_create(const qg_decoder_dims* d, const qg_decoder_layer* layers,
+                           const float* final_norm, const uint8_t* head, const uint8_t* head_meta,
+                           void* workspace, void* exchange, const void* nccl_id, qg_decoder* out) {
   if (!dims_ok(d) || layers == nullptr || final_norm == nullptr || head == nullptr ||
       workspace == nullptr || out == nullptr || (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0u ||
-      (d->tp_size > 1u && nccl_id == nullptr)) {
+      (reinterpret_cast<uintptr_t>(exchange) & 255u) != 0u || (d->tp_size > 1u && nccl_id == nullptr)) {
     return cudaErrorInvalidValue;
   }
   *out = nullptr;
@@ -312,7 +357,7 @@ cudaError_t qg_decoder_create(const qg_decoder_dims* d, const qg_decoder_layer* 
       delete dec;
       return cudaErrorUnknown;
     }
-    const cudaError_t e = exchange_setup(dec);
+    const cudaError_t e = exchange_setup(dec, exchange);
     if (e != cudaSuccess) {
       exchange_teardown(dec);
       ncclCommDestroy(dec->comm);
@@ -324,6 +369,31 @@ cudaError_t qg_decoder_create(const qg_decoder_dims* d, const qg_decoder_layer* 
   return cudaSuccess;
 }
 
+}  // namespace
+
+extern "C" {
+
+cudaError_t qg_decoder_exchange_bytes(const qg_decoder_dims* d, size_t* bytes) {
+  if (!dims_ok(d) || bytes == nullptr) return cudaErrorInvalidValue;
+  *bytes = d->tp_size > 1u ? exchange_bytes(*d) : 0u;
+  return cudaSuccess;
+}
+
+cudaError_t qg_decoder_create(const qg_decoder_dims* d, const qg_decoder_layer* layers,
+                              const float* final_norm, const uint8_t* head,
+                              const uint8_t* head_meta, void* workspace, const void* nccl_id,
+                              qg_decoder* out) {
+  return decoder_create(d, layers, final_norm, head, head_meta, workspace, nullptr, nccl_id, out);
+}
+
+cudaError_t qg_decoder_create_in(const qg_decoder_dims* d, const qg_decoder_layer* layers,
+                                 const float* final_norm, const uint8_t* head,
+                                 const uint8_t* head_meta, void* workspace, void* exchange,
+                                 const void* nccl_id, qg_decoder* out) {
+  if (d != nullptr && d->tp_size > 1u && exchange == nullptr) return cudaErrorInvalidValue;
+  return decoder_create(d, layers, final_norm, head, head_meta, workspace, exchange, nccl_id, out);
+}
+
 cudaError_t qg_decoder_destroy(qg_decoder dec) {
   if (dec == nullptr) return cudaSuccess;
   cudaError_t e = cudaSuccess;
@@ -333,11 +403,17 @@ cudaError_t qg_decoder_destroy(qg_decoder dec) {
   return e;
 }
 
-cudaError_t qg_decoder_step(qg_decoder dec, const float* x, uint32_t pos, uint32_t* token,
-                            cudaStream_t stream) {
-  if (dec == nullptr || x == nullptr || token == nullptr || pos >= dec->dims.ctx_max) {
-    return cudaErrorInvalidValue;
-  }
+}  // extern "C"
+
+namespace {
+
+// One decode step.  pos_dev == nullptr: the position is `pos` (host value, baked into
+// the launches); else *pos_dev is read on the device, ctx_bucket (>= 1) bounds the
+// context the attention grid covers, and `advance` != 0 increments *pos_dev after the
+// token is chosen.
+cudaError_t decoder_step(qg_decoder dec, const float* x, uint32_t pos, uint32_t* pos_dev,
+                         uint32_t ctx_bucket, uint32_t advance, uint32_t* token,
+                         cudaStream_t stream) {
   if (dec->broken) return cudaErrorIllegalState;
   const qg_decoder_dims& d = dec->dims;
   const Shape& s = dec->shape;
@@ -427,9 +503,11 @@ cudaError_t qg_decoder_step(qg_decoder dec, const float* x, uint32_t pos, uint32
       QG_TRY(qg::launch_gemv_multi(d.attn_fmt, 3, p, m, y, r, d.hidden, h, w + L.act_x, stream));
     }
     QG_TRY(qg::launch_rope_append(q, k, v, W.k_cache, W.v_cache, s.nq_local, s.nkv_local,
-                                  d.ctx_max, pos, d.rope_base, stream));
+                                  d.ctx_max, pos, pos_dev, pos_dev ? ctx_bucket : d.ctx_max,
+                                  d.rope_base, stream));
     QG_TRY(qg::launch_attention(q, W.k_cache, W.v_cache, s.nq_local, s.nkv_local, d.ctx_max,
-                                pos + 1u, F(L.partial), attn, w + L.act_attn, stream));
+                                pos_dev ? ctx_bucket : pos + 1u, pos_dev, F(L.partial), attn,
+                                w + L.act_attn, stream));
     QG_TRY(project_out(d.attn_fmt, W.wo, W.wo_meta, attn, w + L.act_attn, x1, cur, s.q_local,
                        dec->canon_o));
     // feed-forward block (the exchange of Wo is gathered into x1)
@@ -465,9 +543,32 @@ cudaError_t qg_decoder_step(qg_decoder dec, const float* x, uint32_t pos, uint32
   if (tp) {
     QG_TRY(nccl_status(ncclAllGather(cand + 2u * d.tp_rank, cand, 2, ncclUint32, dec->comm, stream)));
   }
-  QG_TRY(qg::launch_select_token(cand, d.tp_size, token, stream));
+  QG_TRY(qg::launch_select_token(cand, d.tp_size, token, (pos_dev && advance) ? pos_dev : nullptr,
+                                 stream));
 #undef QG_TRY
   return cudaSuccess;
+}
+
+}  // namespace
+
+extern "C" {
+
+cudaError_t qg_decoder_step(qg_decoder dec, const float* x, uint32_t pos, uint32_t* token,
+                            cudaStream_t stream) {
+  if (dec == nullptr || x == nullptr || token == nullptr || pos >= dec->dims.ctx_max) {
+    return cudaErrorInvalidValue;
+  }
+  return decoder_step(dec, x, pos, nullptr, 0u, 0u, token, stream);
+}
+
+cudaError_t qg_decoder_step_at(qg_decoder dec, const float* x, uint32_t* pos_dev,
+                               uint32_t ctx_bucket, uint32_t advance, uint32_t* token,
+                               cudaStream_t stream) {
+  if (dec == nullptr || x == nullptr || token == nullptr || pos_dev == nullptr ||
+      ctx_bucket == 0u || ctx_bucket > dec->dims.ctx_max) {
+    return cudaErrorInvalidValue;
+  }
+  return decoder_step(dec, x, 0u, pos_dev, ctx_bucket, advance, token, stream);
 }
 
 cudaError_t qg_decoder_views(qg_decoder dec, float** hidden_out, float** logits) {

@@ -76,7 +76,10 @@ SIGNATURES: dict[str, list] = {
     "qg_decoder_workspace_bytes": [P, P],
     "qg_decoder_shard": [P, P, P, P, P, P],
     "qg_decoder_create": [P, P, P, P, P, P, P, P],
+    "qg_decoder_exchange_bytes": [P, P],
+    "qg_decoder_create_in": [P, P, P, P, P, P, P, P, P],
     "qg_decoder_step": [P, P, U32, P, P],
+    "qg_decoder_step_at": [P, P, P, U32, U32, P, P],
     "qg_decoder_views": [P, P, P],
     "qg_decoder_destroy": [P],
 }

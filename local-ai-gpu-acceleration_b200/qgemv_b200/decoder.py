@@ -259,7 +259,8 @@ class Decoder:
     """One rank's decoder: device-resident shards, workspace and the qg_decoder."""
 
     def __init__(self, spec: ModelSpec, weights: dict, rank: int = 0, tp: int = 1,
-                 nccl_id: bytes | None = None, device="cuda", collective: int = COLLECTIVE_NVLINK):
+                 nccl_id: bytes | None = None, device="cuda", collective: int = COLLECTIVE_NVLINK,
+                 exchange: torch.Tensor | None = None):
         self.spec, self.rank, self.tp = spec, rank, tp
         self.device = torch.device(device)
         self._keep = []
@@ -306,13 +307,32 @@ class Decoder:
         idbuf = None
         if tp > 1:
             idbuf = ctypes.create_string_buffer(bytes(nccl_id), 128)
-        check("qg_decoder_create", ctypes.byref(self.dims), arr, fnorm.data_ptr(), head_p, head_m,
-              self.workspace.data_ptr(), idbuf, ctypes.byref(self.handle))
+        if exchange is None:
+            check("qg_decoder_create", ctypes.byref(self.dims), arr, fnorm.data_ptr(), head_p, head_m,
+                  self.workspace.data_ptr(), idbuf, ctypes.byref(self.handle))
+        else:  # caller-owned exchange region (qg_decoder_create_in)
+            self._keep.append(exchange)
+            check("qg_decoder_create_in", ctypes.byref(self.dims), arr, fnorm.data_ptr(), head_p,
+                  head_m, self.workspace.data_ptr(), exchange.data_ptr(), idbuf,
+                  ctypes.byref(self.handle))
 
     def step(self, x: torch.Tensor, pos: int, stream=None) -> torch.Tensor:
         s = (stream or torch.cuda.current_stream(self.device)).cuda_stream
         check("qg_decoder_step", self.handle, x.data_ptr(), pos, self.token.data_ptr(), s)
         return self.token
+
+    def step_at(self, x: torch.Tensor, pos_dev: torch.Tensor, ctx_bucket: int, advance: bool = True,
+                stream=None) -> torch.Tensor:
+        """The step with the position read from pos_dev (a 1-element int32 device tensor)."""
+        s = (stream or torch.cuda.current_stream(self.device)).cuda_stream
+        check("qg_decoder_step_at", self.handle, x.data_ptr(), pos_dev.data_ptr(), ctx_bucket,
+              1 if advance else 0, self.token.data_ptr(), s)
+        return self.token
+
+    def exchange_bytes(self) -> int:
+        n = ctypes.c_size_t(0)
+        check("qg_decoder_exchange_bytes", ctypes.byref(self.dims), ctypes.byref(n))
+        return n.value
 
     def hidden(self) -> torch.Tensor:
         hp, lp = c_void_p(), c_void_p()
@@ -330,6 +350,13 @@ class Decoder:
             self.close()
         except Exception:
             pass
+
+
+def exchange_bytes(spec: ModelSpec, rank: int, tp: int) -> int:
+    n = ctypes.c_size_t(0)
+    d = dims_struct(spec, rank, tp)
+    check("qg_decoder_exchange_bytes", ctypes.byref(d), ctypes.byref(n))
+    return n.value
 
 
 def nccl_unique_id() -> bytes:

@@ -53,20 +53,38 @@ def sanitize_label(name: str) -> str:
     return re.sub(r"[^A-Za-z0-9_.-]+", "_", name)
 
 
-def _role(name: str) -> tuple[int, str]:
+def _role(name: str) -> tuple[int | None, str]:
     m = _LAYER_RE.match(name)
     if m:
         return int(m.group("layer")), m.group("role")
-    return -1, name
+    return None, name  # written as null, which the loaders read as layer -1
+
+
+# Offsets of the tensors in their (GGUF) source file.  The loaders require a non-zero
+# offset; packs made without a source file are given the offsets a GGUF data section
+# starting at 1 MiB with 32-byte alignment would give them.
+_SOURCE_BASE = 1 << 20
+
+
+def _source_offsets(sizes: list[int], offsets: list[int] | None) -> list[int]:
+    if offsets is not None:
+        return list(offsets)
+    out, at = [], _SOURCE_BASE
+    for n in sizes:
+        out.append(at)
+        at += (n + 31) // 32 * 32
+    return out
 
 
 def write_raw_manifest(out_dir: Path, tensors: list[tuple[str, packs.Pack]], model: str = "synthetic",
-                       tensor_plan: str = "synthetic") -> Path:
-    """IQ2_S / IQ3_S / Q5_K raw-block packs and their manifest.json; returns its path."""
+                       tensor_plan: str = "synthetic", source_offsets: list[int] | None = None) -> Path:
+    """IQ2_S / IQ3_S / Q5_K raw-block packs and their manifest.json; returns its path.
+    `source_offsets`: the tensors' offsets in their source file (GGUF ingest)."""
     out_dir = Path(out_dir)
     out_dir.mkdir(parents=True, exist_ok=True)
     rows_out, types = [], set()
-    for name, pk in tensors:
+    offs = _source_offsets([pk.payload.size for _, pk in tensors], source_offsets)
+    for (name, pk), src_off in zip(tensors, offs):
         ttype = TYPE_OF_FORMAT[pk.fmt]
         if ttype == "Q4_K":
             raise ValueError("Q4_K tensors use write_q4k_manifest")
@@ -81,7 +99,7 @@ def write_raw_manifest(out_dir: Path, tensors: list[tuple[str, packs.Pack]], mod
             "name": name, "type": ttype, "layer": layer, "role": role,
             "dimensions": [pk.cols, pk.rows], "element_count": pk.rows * pk.cols,
             "block_size": 256, "block_type_size": BLOCK_TYPE_SIZE[ttype],
-            "block_count": pk.rows * pk.cols // 256, "source_offset": 0,
+            "block_count": pk.rows * pk.cols // 256, "source_offset": int(src_off),
             "source_bytes": int(payload.size), "source_checksum": cs,
             "payload_path": str(path), "payload_bytes": int(payload.size), "payload_checksum": cs,
             "resident_bytes": int(payload.size), "policy": "raw-blocks",
@@ -103,13 +121,14 @@ def write_raw_manifest(out_dir: Path, tensors: list[tuple[str, packs.Pack]], mod
 
 def write_q4k_manifest(out_dir: Path, tensors: list[tuple[str, packs.Pack]], policy: str,
                        write_blocks: bool = True, model: str = "synthetic",
-                       tensor_plan: str = "synthetic") -> Path:
+                       tensor_plan: str = "synthetic", source_offsets: list[int] | None = None) -> Path:
     """Q4_K split packs (payload + metadata of `policy`) from raw Q4_K packs."""
     out_dir = Path(out_dir)
     out_dir.mkdir(parents=True, exist_ok=True)
     fmt, tag = Q4K_POLICIES[policy]
     rows_out = []
-    for name, pk in tensors:
+    offs = _source_offsets([pk.payload.size for _, pk in tensors], source_offsets)
+    for (name, pk), src_off in zip(tensors, offs):
         if pk.fmt != packs.Q4K_RAW:
             raise ValueError("write_q4k_manifest takes raw Q4_K packs")
         blocks = np.ascontiguousarray(pk.payload, np.uint8)
@@ -126,7 +145,7 @@ def write_q4k_manifest(out_dir: Path, tensors: list[tuple[str, packs.Pack]], pol
         res = int(s_payload.size + s_meta.size)
         rows_out.append({
             "name": name, "dimensions": [pk.cols, pk.rows], "rows": pk.rows, "cols": pk.cols,
-            "block_count": pk.rows * pk.cols // 256, "source_offset": 0,
+            "block_count": pk.rows * pk.cols // 256, "source_offset": int(src_off),
             "source_bytes": int(blocks.size), "source_checksum": checksum(blocks),
             "policy": policy, "metadata_format": tag, "payload_path": str(p_path),
             "payload_bytes": int(s_payload.size), "payload_checksum": checksum(s_payload),

@@ -95,6 +95,64 @@ def test_decoder_graph_replay_matches_eager(cuda):
     dec.close()
 
 
+def test_step_at_matches_step_and_replays_across_tokens(cuda):
+    """The step with its position in device memory: bit-identical to the host-position
+    step; one graph captured per context bucket, replayed for successive tokens with the
+    position advanced on the device, equals the eager steps; a position past the bucket
+    writes nothing and sets QG_ERR_POSITION."""
+    from qgemv_b200 import decoder, ops
+    from qgemv_b200.slice import StepGraph
+
+    spec = decoder.ModelSpec(**SMALL)
+    model = decoder.HostModel.synthetic(spec, seed=31)
+    a = decoder.Decoder(spec, copy.deepcopy(decoder.rank_weights(model, 0, 1)))
+    b = decoder.Decoder(spec, copy.deepcopy(decoder.rank_weights(model, 0, 1)))
+    x = torch.randn(spec.hidden, device=cuda)
+    pos = torch.zeros(1, dtype=torch.int32, device=cuda)
+    for p in (0, 9, 40, 63):  # eager: device position vs host position, no advance
+        pos.fill_(p)
+        tb = int(b.step_at(x, pos, ctx_bucket=64, advance=False).item())
+        ta = int(a.step(x, p).item())
+        torch.cuda.synchronize()
+        assert ta == tb and torch.equal(a.hidden(), b.hidden()), p
+        assert int(pos.item()) == p
+    # buckets: a 32-position graph for tokens 10..12, then a 64-position graph for 33, 34
+    stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
+    pos.fill_(10)
+    torch.cuda.synchronize()
+    graphs = {c: StepGraph(stream, lambda c=c: b.step_at(x, pos, ctx_bucket=c, advance=True, stream=stream))
+              for c in (32, 64)}
+    for p in (10, 11, 12):
+        graphs[32].launch()
+        stream.synchronize()
+        ta = int(a.step(x, p).item())
+        torch.cuda.synchronize()
+        assert int(b.token.item()) == ta and torch.equal(a.hidden(), b.hidden()), p
+    assert int(pos.item()) == 13
+    pos.fill_(33)
+    torch.cuda.synchronize()
+    for p in (33, 34):
+        graphs[64].launch()
+        stream.synchronize()
+        ta = int(a.step(x, p).item())
+        torch.cuda.synchronize()
+        assert int(b.token.item()) == ta and torch.equal(a.hidden(), b.hidden()), p
+    assert ops.get_error() == 0
+    # position 40 in the 32-position bucket: refused on the device, caches untouched
+    caches = [c.clone() for c in b.caches[0]]
+    pos.fill_(40)
+    torch.cuda.synchronize()
+    graphs[32].launch()
+    stream.synchronize()
+    assert ops.get_error() & 0x2  # QG_ERR_POSITION
+    assert all(torch.equal(c, d) for c, d in zip(caches, b.caches[0]))
+    for g in graphs.values():
+        g.close()
+    a.close()
+    b.close()
+
+
 TP_STEPS = (30, 31, 32)  # positions; the middle step runs as a captured graph
 
 
@@ -120,7 +178,7 @@ def _run_steps(dec, spec, dev):
     return out
 
 
-def _tp_rank(rank, world, q_in, q_out, spec_kw, collective):
+def _tp_rank(rank, world, q_in, q_out, spec_kw, collective, caller_exchange=False):
     sys.path.insert(0, str(REPO / "local-ai-gpu-acceleration_b200"))
     import torch
 
@@ -136,17 +194,25 @@ def _tp_rank(rank, world, q_in, q_out, spec_kw, collective):
     else:
         nid = q_in.get(timeout=120)
     dev = f"cuda:{rank}"
+    exchange = None
+    if caller_exchange:
+        # the exchange region inside a larger caller allocation, at a 256-B offset (the way
+        # a superallocator arena sits inside its pool)
+        n = decoder.exchange_bytes(spec, rank, world)
+        pool = torch.zeros(n + 4096, dtype=torch.uint8, device=dev)
+        exchange = pool[768 + 256 * rank:][:n]
     dec = decoder.Decoder(spec, decoder.rank_weights(model, rank, world), rank=rank, tp=world,
-                          nccl_id=nid, device=dev, collective=collective)
+                          nccl_id=nid, device=dev, collective=collective, exchange=exchange)
     out = _run_steps(dec, spec, dev)
     q_out.put((rank, out, ops.get_error()))
     dec.close()
 
 
-@pytest.mark.parametrize("world,spec_kw,collective", [
-    (2, SMALL, 0), (2, SMALL, 1), (4, SMALL_TP4, 0), (8, SMALL_TP8, 0)],
-    ids=["tp2", "tp2-nccl", "tp4", "tp8"])
-def test_decoder_tp_matches_oracle_and_tp1(port, world, spec_kw, collective):
+@pytest.mark.parametrize("world,spec_kw,collective,caller_exchange", [
+    (2, SMALL, 0, False), (2, SMALL, 1, False), (2, SMALL, 0, True), (4, SMALL_TP4, 0, False),
+    (8, SMALL_TP8, 0, False)],
+    ids=["tp2", "tp2-nccl", "tp2-caller-exchange", "tp4", "tp8"])
+def test_decoder_tp_matches_oracle_and_tp1(port, world, spec_kw, collective, caller_exchange):
     """World ranks over NVLink (exchange fused into the Wo / Wd GEMVs; or, tp2-nccl, the
     same exchange words moved by ncclAllGather): three consecutive steps -- eager, captured
     graph, eager -- against the oracle stepping the same model with its caches carried
@@ -168,8 +234,8 @@ def test_decoder_tp_matches_oracle_and_tp1(port, world, spec_kw, collective):
     ctx = mp.get_context("spawn")
     q_in, q_out = ctx.Queue(), ctx.Queue()
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
-    procs = [ctx.Process(target=_tp_rank, args=(r, world, q_in, q_out, spec_kw, collective))
-             for r in range(world)]
+    procs = [ctx.Process(target=_tp_rank, args=(r, world, q_in, q_out, spec_kw, collective,
+                                                caller_exchange)) for r in range(world)]
     for p in procs:
         p.start()
     res = [q_out.get(timeout=300) for _ in procs]
