@@ -57,6 +57,10 @@ CONFIG = {
     "batch": 1,
     "l2": "no flush: 2.37 GB of packs streamed per step (> 126 MB L2)",
     "entry_point": "qg_act_prepare once per distinct x + qg_gemv_act per GEMV (C-ABI), one CUDA graph per step",
+    "activation_precision": "fp32 x quantized per 32 columns into two int8 planes "
+                            "(x ~= s*(hi + lo/256), |error| <= 3.2e-5*||x||_inf per element) for "
+                            "the batch-1 GEMVs; fp16 (power-of-two scaled per row) on the tcgen05 "
+                            "batched path; fp32 accumulation and fp32 outputs",
 }
 
 

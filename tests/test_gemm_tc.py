@@ -74,7 +74,7 @@ def test_gemm_batched_deterministic_and_scaled_inputs(cuda, port, fmt):
 @pytest.mark.gpu
 @pytest.mark.parametrize("fmt", [packs.Q4K_RAW, packs.IQ2S])
 @pytest.mark.parametrize("rows,cols", [(28672, 8192), (8192, 28672)])
-@pytest.mark.parametrize("batch", [8, 32])
+@pytest.mark.parametrize("batch", [8, 16, 32])
 def test_gemm_batched_config4_sampled_rows(cuda, port, fmt, rows, cols, batch):
     """BASELINE config 4 shapes in full on the GPU; three 16-row windows against the oracle."""
     pk = packs.synthetic_pack(fmt, rows, cols, seed=rows + cols + fmt)
