@@ -428,6 +428,43 @@ cudaError_t qg_decoder_step_at(qg_decoder dec, const float* x, uint32_t* pos_dev
 cudaError_t qg_decoder_views(qg_decoder dec, float** hidden, float** logits);
 cudaError_t qg_decoder_destroy(qg_decoder dec);
 
+/* ---------------------------------------------------------------------------
+ * GGUF ingest (host code; the reference's reader is runtime/apps/gguf_probe/main.cpp:124-631):
+ * header, metadata (general.alignment, general.architecture), tensor infos, the data
+ * section offset, tensor spans and the probe's validation (supported ggml type, block-
+ * aligned element count, span >= expected bytes with padding < alignment).  Tensor bytes
+ * are read into host memory; qgemv_b200/manifest.py writes them as resident packs.
+ * Errors: cudaErrorFileNotFound (open), cudaErrorInvalidValue (not GGUF, truncated,
+ * bad argument), cudaErrorInvalidSymbol (qg_gguf_find: no such tensor).
+ * ------------------------------------------------------------------------- */
+typedef struct qg_gguf_s* qg_gguf;
+typedef struct qg_gguf_info {
+  uint32_t version;
+  uint64_t tensor_count, metadata_count;
+  uint64_t tensor_info_end_offset, tensor_data_offset, tensor_data_alignment;
+  uint64_t supported_tensors, valid_tensors, expected_data_bytes;
+  char architecture[64];
+} qg_gguf_info;
+typedef struct qg_gguf_tensor_info {
+  char name[256];
+  uint32_t ggml_type;        /* 12 Q4_K, 13 Q5_K, 21 IQ3_S, 22 IQ2_S, 0 F32, 1 F16, 8 Q8_0 */
+  uint32_t n_dims;
+  uint64_t dims[4];          /* GGUF order: dims[0] = columns */
+  uint64_t offset;           /* relative to the data section */
+  uint64_t absolute_offset;  /* in the file */
+  uint64_t span_bytes;       /* to the next tensor (or the end of the file) */
+  uint64_t data_bytes;       /* expected bytes of the type and dims (0: unsupported type) */
+  uint32_t block_size, type_size;
+  uint32_t valid;
+} qg_gguf_tensor_info;
+cudaError_t qg_gguf_open(const char* path, qg_gguf* out);
+cudaError_t qg_gguf_summary(qg_gguf g, qg_gguf_info* info);
+cudaError_t qg_gguf_tensor(qg_gguf g, uint64_t index, qg_gguf_tensor_info* out);
+cudaError_t qg_gguf_find(qg_gguf g, const char* name, uint64_t* index);
+/* `bytes` must equal the tensor's data_bytes; the tensor must be valid. */
+cudaError_t qg_gguf_read(qg_gguf g, uint64_t index, void* dst, uint64_t bytes);
+cudaError_t qg_gguf_close(qg_gguf g);
+
 /* Reads the library's device error word (QG_ERR_* bits) for the current device and
  * clears it.  Synchronizes the device.  Returns the cudaError_t of the read. */
 cudaError_t qg_get_error(uint32_t* error_bits);

@@ -82,6 +82,12 @@ SIGNATURES: dict[str, list] = {
     "qg_decoder_step_at": [P, P, P, U32, U32, P, P],
     "qg_decoder_views": [P, P, P],
     "qg_decoder_destroy": [P],
+    "qg_gguf_open": [ctypes.c_char_p, P],
+    "qg_gguf_summary": [P, P],
+    "qg_gguf_tensor": [P, U64, P],
+    "qg_gguf_find": [P, ctypes.c_char_p, P],
+    "qg_gguf_read": [P, U64, P, U64],
+    "qg_gguf_close": [P],
 }
 
 _LIB: ctypes.CDLL | None = None
