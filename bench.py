@@ -326,12 +326,23 @@ def measure_reference_gpu(device, mats, xs, args) -> dict | None:
 BATCHED_FORMATS = [packs.Q4K_RAW, packs.IQ2S]
 BATCHED_SHAPES = [(28672, 8192), (8192, 28672)]
 BATCHED_SIZES = [1, 8, 16, 32]
+# first batch qg_gemm_batched runs on the tensor cores (the library reads the same variable)
+TC_MIN_BATCH = int(os.environ.get("QG_TC_MIN_BATCH", "5"))
+
+
+def batch_slices(fmt: int, batch: int, rows: int, cols: int) -> int:
+    """Column slices (= launches per 8-vector group) of the multi-vector GEMV: 8 warps of
+    32 sub-blocks per slice with 5..8 vectors, 16 warps with 2..4."""
+    kb = cols // 256
+    per = 4 * (8 if min(batch, 8) > 4 else 16)
+    return -(-kb // per)
 
 
 def measure_batched(device, args, peak: float, only: tuple | None = None) -> dict:
     """{Q4_K, IQ2_S} x {28672x8192, 8192x28672} at batch 1, 8, 16, 32.
-    Batch 1 is the GEMV (qg_act_prepare + qg_gemv_act); batch >= 2 is qg_gemm_batched
-    (tensor cores).  Each graph replay walks a rotation of pack copies totalling >= 400 MB,
+    Batch 1 is the GEMV (qg_act_prepare + qg_gemv_act); batch 2..15 is qg_gemm_batched's
+    CUDA-core multi-vector GEMV (one weight pass per 8 vectors, one launch per column
+    slice), batch >= 16 its tensor-core path.  Each graph replay walks a rotation of pack copies totalling >= 400 MB,
     so no call finds its weights in L2; time per call = replay time / copies."""
     import torch
 
@@ -366,7 +377,7 @@ def measure_batched(device, args, peak: float, only: tuple | None = None) -> dic
 
                     def call(p, x=x, y=y, ws=ws, batch=batch):
                         ops.gemm_batched(fmt, p, None, x, rows, cols, y=y, workspace=ws, stream=stream)
-                    launches = 3
+                    launches = 3 if batch >= TC_MIN_BATCH else -(-batch // 8) * batch_slices(fmt, batch, rows, cols)
                 with torch.cuda.stream(stream):
                     for p in payloads:  # eager warm-up: kernel attributes
                         call(p)
@@ -392,7 +403,8 @@ def measure_batched(device, args, peak: float, only: tuple | None = None) -> dic
                 gbps = nbytes / (us * 1e-6) / 1e9
                 cases.append({
                     "fmt": packs.FORMAT_NAMES[fmt], "rows": rows, "cols": cols, "batch": batch,
-                    "path": "gemv" if batch == 1 else "tcgen05", "us": round(us, 2),
+                    "path": "gemv" if batch == 1 else "tcgen05" if batch >= TC_MIN_BATCH else "cuda-core multi-vector",
+                    "us": round(us, 2),
                     "weight_GBps": round(gbps, 1), "frac_hbm": round(gbps / peak, 3),
                     "TFLOPs": round(2.0 * rows * cols * batch / (us * 1e-6) / 1e12, 2),
                     "launches": launches,

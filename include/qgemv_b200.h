@@ -242,7 +242,11 @@ cudaError_t qg_decode_stage(int fmt, const uint8_t* payload, const uint8_t* meta
                             uint32_t page_words, uint32_t active_pages, cudaStream_t stream);
 
 /* Y[b, r] = sum_c W[r, c] * X[b, c] for b < batch (X row-major [batch, cols] fp32,
- * Y row-major [batch, rows]).  batch 1..32. */
+ * Y row-major [batch, rows]).  batch 1..32, every format.  On the CUDA cores: each group
+ * of up to 8 vectors is one pass over the weights (multi-vector GEMV, csrc/qg_gemv_batch.cu:
+ * x as int16 with one scale per vector and column slice, |error| <= 1.6e-5 *
+ * ||w_row||_1 * ||x_b||_inf plus fp32 rounding; deterministic); a single vector takes the
+ * batch-1 GEMV.  Packs whose payload or metadata is not 16-B aligned go vector by vector. */
 cudaError_t qg_gemv_batched(int fmt, const uint8_t* payload, const uint8_t* meta,
                             const float* x, float* y, uint32_t batch, uint32_t rows,
                             uint32_t cols, cudaStream_t stream);
@@ -261,9 +265,11 @@ cudaError_t qg_argmax_token(const float* values, uint32_t n, uint32_t* token,
                             uint32_t token_offset, uint32_t add_token, uint32_t modulus,
                             cudaStream_t stream);
 
-/* Batched GEMM on the tensor cores (no reference counterpart -- every
- * reference matvec kernel is batch 1): Y[b, r] = sum_c W[r, c] * X[b, c] for b < batch,
- * X row-major [batch, cols] fp32, Y row-major [batch, rows] fp32, batch 1..32.
+/* Batched decode GEMM (no reference counterpart -- every reference matvec kernel is
+ * batch 1): Y[b, r] = sum_c W[r, c] * X[b, c] for b < batch, X row-major [batch, cols]
+ * fp32, Y row-major [batch, rows] fp32, batch 1..32.  Below batch 5 it runs the CUDA-core
+ * multi-vector GEMV of qg_gemv_batched (workspace unused); from batch 5 the tensor cores
+ * (the crossover measured on B200; the QG_TC_MIN_BATCH environment variable, 2..33, moves it):
  * Formats: QG_FMT_Q4K_RAW, QG_FMT_Q5K, QG_FMT_IQ2S, QG_FMT_IQ3S (payload 16-B aligned;
  * `meta` unused).  Weights are expanded to exact fp16 integer tiles and contracted
  * with tcgen05.mma (M=128, N=16 or 32) against x scaled by a power of two per batch row

@@ -248,13 +248,7 @@ cudaError_t qg_gemv_batched(int fmt, const uint8_t* payload, const uint8_t* meta
   if (!gemv_args_ok(fmt, payload, meta, x, y, rows, cols) || batch == 0u || batch > 32u) {
     return cudaErrorInvalidValue;
   }
-  for (uint32_t b = 0; b < batch; ++b) {
-    const cudaError_t e = qg::launch_gemv(fmt, payload, meta, x + static_cast<uint64_t>(b) * cols,
-                                          nullptr, y + static_cast<uint64_t>(b) * rows, nullptr,
-                                          nullptr, nullptr, 0u, 0u, 0u, rows, cols, stream);
-    if (e != cudaSuccess) return e;
-  }
-  return cudaSuccess;
+  return qg::launch_gemv_vectors(fmt, payload, meta, x, y, batch, rows, cols, stream);
 }
 
 cudaError_t qg_act_bytes(uint32_t cols, size_t* bytes) {

@@ -50,6 +50,7 @@
 #include <cudaTypedefs.h>
 #include <cuda_fp16.h>
 
+#include <cstdlib>
 #include <mutex>
 #include <set>
 #include <utility>
@@ -61,6 +62,11 @@ namespace qg {
 namespace {
 
 constexpr uint32_t kTileM = 128;
+// Batch from which qg_gemm_batched uses the tensor cores, set by measurement on B200
+// (Q4_K 28672x8192): the CUDA-core multi-vector GEMV takes 48.6 / 77 / 114 us at batch
+// 2 / 4 / 8, these tiles 80 / 80 / 79 us -- the 8-vector GEMV is bound by the half-rate
+// integer dot-product pipe (4 dp2a per weight).
+constexpr uint32_t kTcMinBatch = 5;
 constexpr uint32_t kBlockCols = 256;
 constexpr uint32_t kA2Bytes = kTileM * 16u * 2u;  // min tile: 128 rows x K=16 fp16
 constexpr uint32_t kXStages = 4;
@@ -116,7 +122,10 @@ struct TcLayout {
   static constexpr uint32_t t_off = x_off + kXStages * xrec;
   static constexpr uint32_t raw_off = (t_off + F::table_bytes + 1023u) & ~1023u;
   static constexpr uint32_t raw_stage = kTileM * F::rowb;
-  static constexpr uint32_t misc = 512;  // barriers, tensor-memory address, flags
+  // barriers, tensor-memory address, flags (512 B), then the block scales of the
+  // accumulator slots' units: [kAccSlots][2][128] fp32 (d-scale, dmin per row)
+  static constexpr uint32_t scl_rel = 512;
+  static constexpr uint32_t misc = scl_rel + kAccSlots * 2u * kTileM * 4u;
   static constexpr uint32_t slack = 1024;
   static constexpr uint32_t raw_stages_fit = (kSmemLimit - raw_off - misc - slack) / raw_stage;
   static constexpr uint32_t raw_stages = raw_stages_fit > kMaxRawStages ? kMaxRawStages : raw_stages_fit;
@@ -239,18 +248,6 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t pari
   return ok != 0u;
 }
 
-__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_addr(bar)), "r"(parity)
-      : "memory");
-  return ok != 0u;
-}
-
 // Bounded wait of at most kMaxTcPolls suspended polls; gives up early once another
 // role has set the CTA's abort flag.
 __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, volatile uint32_t* abort) {
@@ -265,19 +262,21 @@ __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, volatile
 
 // Spinning variant for the MMA-issuing thread, the pipeline's critical path: a
 // non-blocking poll of a completed phase costs a few cycles where a suspending one can
-// cost hundreds under load.  Bounded like tc_wait.
-__device__ __forceinline__ bool tc_spin(uint64_t* bar, uint32_t parity, volatile uint32_t* abort) {
-  for (uint32_t it = 0; it < kMaxSpinPolls; ++it) {
-    if (mbar_test_wait(bar, parity)) return true;
-    if ((it & 1023u) == 1023u && *abort != 0u) return false;
-  }
-  atomicOr(&g_error_word, QG_ERR_WAIT_TIMEOUT);
-  *abort = 1u;
-  return false;
+// cost hundreds under load (measured on B200: Q4_K 28672x8192 at batch 16 takes 79.5 us
+// with this spin, 88 us with suspending try_waits).  Up to three phases at once (b1 may
+// be null): the polls are independent, so their latencies overlap.
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0u;
 }
 
-// Up to three phases at once (b1 may be null): the polls are independent, so their
-// latencies overlap.  Bounded like tc_spin.
 __device__ __forceinline__ bool tc_spin3(uint64_t* b1, uint32_t p1, uint64_t* b2, uint32_t p2, uint64_t* b3,
                                          uint32_t p3, volatile uint32_t* abort) {
   bool ok1 = b1 == nullptr, ok2 = false, ok3 = false;
@@ -296,7 +295,7 @@ __device__ __forceinline__ bool tc_spin3(uint64_t* b1, uint32_t p1, uint64_t* b2
   return false;
 }
 
-// The same wait done by lane 0 for the whole warp.
+// Warp-wide tc_wait: lane 0 waits, the warp learns the outcome.
 __device__ __forceinline__ bool tc_wait_warp(uint64_t* bar, uint32_t parity, volatile uint32_t* abort,
                                              uint32_t lane) {
   uint32_t ok = 0;
@@ -619,8 +618,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
   uint64_t* unit_done = x_full + kXStages; // per unit ring index: all MMAs of the unit completed
   uint64_t* acc_empty = unit_done + kXStages;
   uint64_t* done = acc_empty + kAccSlots;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  uint64_t* scale_full = done + 1;          // per accumulator slot: the unit's block scales written
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(scale_full + kAccSlots);
   volatile uint32_t* abort = tmem_slot + 1;
+  float* scales = reinterpret_cast<float*>(sm + L::bar_off + L::scl_rel);
 
   const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31u;
   const uint64_t u0 = range_start(args.units, args.grid, blockIdx.x);
@@ -643,6 +644,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
       mbar_init(&acc_empty[i], 4);  // one arrival per epilogue warp
     }
     mbar_init(done, 1);
+    for (uint32_t i = 0; i < kAccSlots; ++i) mbar_init(&scale_full[i], 4);  // the h = 0 dequantize warps
     *abort = 0u;
     fence_mbar_init();
   }
@@ -808,7 +810,21 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
       // dequantize whatever their slot holds, and their results are never written
       uint32_t off = 0;
       if constexpr (F::window) off = static_cast<uint32_t>(((static_cast<uint64_t>(row) * kb + k) * F::bpb) & 15u);
-      Dequant<FMT>::run(sRaw + s * L::raw_stage + r * F::rowb + off, h, r, A2, sT, emit);
+      const uint8_t* blk = sRaw + s * L::raw_stage + r * F::rowb + off;
+      if (h == 0u) {
+        // The unit's block scales for the epilogue, from the staged block (the weight
+        // stream is L2 evict-first, so re-reading them from global memory would go to
+        // DRAM once per row and unit).  Slot t is free once the epilogue released unit
+        // n - kAccSlots.
+        const uint32_t t = n % kAccSlots;
+        if (n >= kAccSlots && !tc_wait_warp(&acc_empty[t], ((n / kAccSlots) & 1u) ^ 1u, abort, lane)) break;
+        const float d = h2f(lds_u16(blk));
+        scales[(t * 2u) * kTileM + r] = FMT == QG_FMT_IQ2S ? d * 0.125f : d;
+        scales[(t * 2u + 1u) * kTileM + r] = F::has_min ? h2f(lds_u16(blk + 2)) : 0.f;
+        __syncwarp();
+        if (lane == 0u) mbar_arrive(&scale_full[t]);
+      }
+      Dequant<FMT>::run(blk, h, r, A2, sT, emit);
       tmem_wait_st();
       if (F::has_min && h == 1u) fence_proxy_async_smem();  // min tile -> tensor core
       tc_fence_before();
@@ -830,16 +846,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
       const uint32_t tile = static_cast<uint32_t>(u / kb), k = static_cast<uint32_t>(u % kb);
       const uint32_t row = tile * kTileM + r;
       const uint32_t t = n % kAccSlots;
-      // block scales, loaded before the wait so their latency overlaps it
-      float dq = 0.f, dm = 0.f;
-      if (row < args.rows) {
-        const uint8_t* blk = args.payload + (static_cast<uint64_t>(row) * kb + k) * F::bpb;
-        const float d = h2f(*reinterpret_cast<const uint16_t*>(blk));
-        dq = FMT == QG_FMT_IQ2S ? d * 0.125f : d;
-        if constexpr (F::has_min) dm = h2f(*reinterpret_cast<const uint16_t*>(blk + 2));
-      }
       if (!tc_wait_warp(&unit_done[t], (n / kAccSlots) & 1u, abort, lane)) break;
+      if (!tc_wait_warp(&scale_full[t], (n / kAccSlots) & 1u, abort, lane)) break;
       tc_fence_after();
+      // block scales of the unit's rows (written by the dequantize warps)
+      const float dq = scales[(t * 2u) * kTileM + r];
+      const float dm = F::has_min ? scales[(t * 2u + 1u) * kTileM + r] : 0.f;
       const uint32_t taddr = tmem + ((quarter * 32u) << 16) + t * 2u * NB;
 #pragma unroll
       for (uint32_t c = 0; c < NB; c += 16u) {
@@ -1169,6 +1181,19 @@ cudaError_t launch_gemm_tc(int fmt, const uint8_t* payload, const float* x, floa
 
 bool gemm_tc_supports(int fmt) { return tc_format(fmt); }
 
+// First batch size qg_gemm_batched runs on the tensor cores: kTcMinBatch, or the
+// QG_TC_MIN_BATCH environment variable (2..33; 33 keeps every batch on the CUDA cores),
+// read once per process.
+uint32_t tc_min_batch() {
+  static const uint32_t v = [] {
+    const char* e = std::getenv("QG_TC_MIN_BATCH");
+    if (e == nullptr) return kTcMinBatch;
+    const long n = std::strtol(e, nullptr, 10);
+    return n >= 2 && n <= 33 ? static_cast<uint32_t>(n) : kTcMinBatch;
+  }();
+  return v;
+}
+
 }  // namespace qg
 
 extern "C" {
@@ -1191,6 +1216,11 @@ cudaError_t qg_gemm_batched(int fmt, const uint8_t* payload, const uint8_t* meta
       cols % 256u != 0u || (reinterpret_cast<uintptr_t>(payload) & 15u) != 0u ||
       (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0u) {
     return cudaErrorInvalidValue;
+  }
+  // Below the tensor-core threshold the CUDA-core multi-vector GEMV reads each weight once
+  // for up to 8 vectors (qg_gemv_batch.cu); the tensor-core tiles take larger batches.
+  if (batch < qg::tc_min_batch()) {
+    return qg::launch_gemv_vectors(fmt, payload, meta, x, y, batch, rows, cols, stream);
   }
   return qg::launch_gemm_tc(fmt, payload, x, y, batch, rows, cols, workspace, stream);
 }

@@ -70,6 +70,27 @@ cudaError_t launch_gemv_multi(int fmt, uint32_t nseg, const uint8_t* const* payl
                               const uint8_t* const* meta, float* const* y, const uint32_t* rows,
                               uint32_t cols, const float* x, const void* act, cudaStream_t stream);
 
+// Multi-vector GEMV on the CUDA cores (qg_gemv_batch.cu): Y[v] = W X[v] for v < nvec
+// (1..8), X[v] at x + v * x_stride, Y[v] at y + v * y_stride; one launch per column
+// slice, chained on the stream.  Plan of one launch (every slice of a matrix shares it).
+struct BatchPlan {
+  uint32_t slices, warps, q, units, stages, slot_p, slot_m, stage_bytes;
+  uint32_t table_off, red_off, xs_off, stage_off, smem, ok;
+};
+BatchPlan plan_gemv_batch(int fmt, uint32_t nvec, uint32_t rows, uint32_t cols);
+// Shapes and alignments the multi-vector kernel takes (16-B aligned payload / metadata).
+bool gemv_batch_ok(int fmt, const uint8_t* payload, const uint8_t* meta, uint32_t rows, uint32_t cols);
+cudaError_t launch_gemv_batch(int fmt, const uint8_t* payload, const uint8_t* meta, const float* x,
+                              float* y, uint32_t nvec, uint32_t x_stride, uint32_t y_stride,
+                              uint32_t rows, uint32_t cols, cudaStream_t stream);
+// First batch size qg_gemm_batched runs on the tensor cores (QG_TC_MIN_BATCH overrides).
+uint32_t tc_min_batch();
+// Y = W X for `batch` vectors (X [batch][cols], Y [batch][rows]) on the CUDA cores:
+// one weight pass per group of up to 8 vectors.
+cudaError_t launch_gemv_vectors(int fmt, const uint8_t* payload, const uint8_t* meta, const float* x,
+                                float* y, uint32_t batch, uint32_t rows, uint32_t cols,
+                                cudaStream_t stream);
+
 // Bytes of a prepared activation of `cols` values (176 per 64 columns).
 inline size_t act_bytes(uint32_t cols) { return static_cast<size_t>(cols / 64u) * 176u; }
 cudaError_t launch_act_prepare(const float* x, uint32_t cols, void* act, cudaStream_t stream);

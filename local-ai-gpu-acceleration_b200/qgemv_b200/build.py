@@ -12,7 +12,7 @@ PKG_DIR = Path(__file__).resolve().parents[1]          # local-ai-gpu-accelerati
 CSRC = PKG_DIR / "csrc"
 LIB_PATH = PKG_DIR / "libqgemv_b200.so"
 SOURCES = ["qg_gemv.cu", "qg_aux.cu", "qg_abi.cu", "qg_slice.cu", "qg_attn.cu", "qg_decode.cu",
-           "qg_noalloc.cu", "qg_gemm_tc.cu", "qg_gguf.cu"]
+           "qg_noalloc.cu", "qg_gemm_tc.cu", "qg_gguf.cu", "qg_gemv_batch.cu"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
