@@ -2,14 +2,21 @@
 // counterpart: the reference's attention kernels are synthetic surrogates,
 // runtime/kernels/decode/decode_kernels.cu:311-1136).
 //
-//  * rope_append_kernel: rotary position embedding of this rank's q and k heads
-//    (adjacent pairs (2i, 2i+1), angle pos * base^(-2i/head_dim)), then k and v of the
-//    new position written to the fp16 KV cache.
-//  * attn_split_tc_kernel (groups <= 8, tensor cores) or attn_split_kernel (CUDA cores)
-//    + attn_combine_kernel: grouped-query decode attention over the fp16 cache
-//    (flash-decoding: one CTA per (kv head, span of positions) computes the span's max,
-//    sum and weighted V for all q heads of the group; the combine merges the spans,
-//    normalises and emits the Wo GEMV's int8 planes).
+//  * Decode attention, two launches per layer: attn_split_tc_kernel (groups <= 8, tensor
+//    cores) or attn_split_kernel (CUDA cores), grouped-query flash-decoding over the fp16
+//    KV cache -- one CTA per (kv head, span of 64 positions) computes the span's max, sum
+//    and weighted V for all q heads of the group -- then attn_combine_kernel, which merges
+//    the spans of every q head in span order, normalises and writes the output and the
+//    Wo GEMV's int8 planes.  The split launch also
+//      - applies the rotary position embedding (adjacent pairs (2i, 2i+1), angle
+//        pos * base^(-2i/head_dim)) to q as it is loaded, from a per-CTA sin/cos table
+//        built while the span's loads are in flight;
+//      - appends the new position: the CTA whose span holds it writes the rotated k row
+//        and the v row to the cache before it reads its span.
+//    (A merge inside the split launch -- the last CTA of each group of spans merging the
+//    group, the last group merging the groups -- measured slower on B200 than the
+//    separate combine: its chain of dependent global round trips (records, fence,
+//    arrival counter, loads) left the SMs idle for 60 % of the launch.)
 //  * argmax_candidate_kernel + select_token_kernel: vocab-sharded argmax (lowest index
 //    wins ties).
 #include <cooperative_groups.h>
@@ -32,49 +39,82 @@ __device__ __forceinline__ uint32_t step_position(uint32_t pos, const uint32_t* 
   return pos_dev != nullptr ? *reinterpret_cast<const volatile uint32_t*>(pos_dev) : pos;
 }
 
-__global__ void rope_append_kernel(float* q, float* k, const float* v, __half* k_cache,
-                                   __half* v_cache, uint32_t n_q, uint32_t n_kv, uint32_t ctx_max,
-                                   uint32_t pos_arg, const uint32_t* pos_dev, uint32_t ctx_limit,
-                                   float rope_base) {
-  pdl_wait();
-  pdl_trigger();
-  const uint32_t pos = step_position(pos_arg, pos_dev);
-  if (pos >= ctx_limit) {  // a position past the cache (or the graph's bucket): no write
-    if (blockIdx.x == 0u && threadIdx.x == 0u) atomicOr(&g_error_word, QG_ERR_POSITION);
-    return;
-  }
-  // one thread per rotation pair of one head (q heads first, then k heads), plus the
-  // v copy done by the k-head threads
-  const uint32_t pairs = kHeadDim / 2u;
-  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
-  const uint32_t head = i / pairs, j = i - head * pairs;
-  if (head >= n_q + n_kv) return;
-  const float inv_freq = powf(rope_base, -2.0f * static_cast<float>(j) / static_cast<float>(kHeadDim));
-  float sn, cs;
-  sincosf(static_cast<float>(pos) * inv_freq, &sn, &cs);
-  float* base = head < n_q ? q + head * kHeadDim : k + (head - n_q) * kHeadDim;
-  const float a = base[2u * j], b = base[2u * j + 1u];
-  const float ra = a * cs - b * sn, rb = a * sn + b * cs;
-  base[2u * j] = ra;
-  base[2u * j + 1u] = rb;
-  if (head >= n_q) {
-    const uint32_t kv = head - n_q;
-    const size_t at = (static_cast<size_t>(kv) * ctx_max + pos) * kHeadDim + 2u * j;
-    k_cache[at] = __float2half_rn(ra);
-    k_cache[at + 1u] = __float2half_rn(rb);
-    v_cache[at] = __float2half_rn(v[kv * kHeadDim + 2u * j]);
-    v_cache[at + 1u] = __float2half_rn(v[kv * kHeadDim + 2u * j + 1u]);
+constexpr uint32_t kRec = kHeadDim + 4u;  // partial record: o[128], max, sum, 2 pad (16-B rows)
+
+// One decode step's attention (the arguments of both split kernels).
+struct AttnStep {
+  const float* q;        // [n_q][128] this rank's q heads, before the rotation
+  const float* k;        // [n_kv][128] the new position's k, before the rotation
+  const float* v;        // [n_kv][128] the new position's v
+  __half* k_cache;       // [n_kv][ctx_max][128]
+  __half* v_cache;
+  float* partial;        // [n_q][spans][kRec] per-span records
+  const uint32_t* pos_dev;
+  uint32_t G, ctx_max, pos_arg, ctx_limit, spans;
+  float rope_base;
+};
+
+// Shared scratch of the prologue: the position's rotation table.
+struct AttnShared {
+  float cs[kHeadDim / 2u], sn[kHeadDim / 2u];
+};
+
+// The rotation table of position pos: angle i = pos * base^(-2i/head_dim).
+__device__ __forceinline__ void rope_table(const AttnStep& a, uint32_t pos, AttnShared& sh) {
+  const uint32_t tid = threadIdx.x;
+  if (tid < kHeadDim / 2u) {
+    const float inv_freq =
+        powf(a.rope_base, -2.0f * static_cast<float>(tid) / static_cast<float>(kHeadDim));
+    sincosf(static_cast<float>(pos) * inv_freq, &sh.sn[tid], &sh.cs[tid]);
   }
 }
 
-cudaError_t launch_rope_append(float* q, float* k, const float* v, void* k_cache, void* v_cache,
-                               uint32_t n_q, uint32_t n_kv, uint32_t ctx_max, uint32_t pos,
-                               const uint32_t* pos_dev, uint32_t ctx_limit, float rope_base,
-                               cudaStream_t stream) {
-  const uint32_t threads = (n_q + n_kv) * (kHeadDim / 2u);
-  return launch_k(rope_append_kernel, (threads + 127u) / 128u, 128, 0, stream, q, k, v,
-                  static_cast<__half*>(k_cache), static_cast<__half*>(v_cache), n_q, n_kv, ctx_max,
-                  pos, pos_dev, ctx_limit < ctx_max ? ctx_limit : ctx_max, rope_base);
+// Everything before the span is read: the position (or QG_ERR_POSITION) and this CTA's
+// context length; in the CTA whose span holds the position, the rotation table and the
+// new k (rotated) and v rows appended to the cache (`owner`).  The other CTAs build the
+// table (rope_table) once their span's loads are in flight.  Returns false when the CTA
+// has no positions (a span of the graph's bucket past this token's context).
+__device__ __forceinline__ bool attn_prologue(const AttnStep& a, uint32_t kv, uint32_t span,
+                                              AttnShared& sh, uint32_t& ctx_len, uint32_t& pos,
+                                              bool& owner) {
+  const uint32_t tid = threadIdx.x;
+  pdl_wait();  // q, k, v come from the previous kernel
+  pdl_trigger();
+  pos = step_position(a.pos_arg, a.pos_dev);
+  if (pos >= a.ctx_limit) {  // a position past the cache (or the graph's bucket): no work
+    if (kv == 0u && span == 0u && tid == 0u) atomicOr(&g_error_word, QG_ERR_POSITION);
+    return false;
+  }
+  ctx_len = pos + 1u;
+  const uint32_t t0 = span * kSpan;
+  if (t0 >= ctx_len) return false;
+  owner = pos < t0 + kSpan;
+  if (owner) {
+    // this CTA's span holds the new position: append it before the span is read
+    rope_table(a, pos, sh);
+    __syncthreads();
+    const size_t at = (static_cast<size_t>(kv) * a.ctx_max + pos) * kHeadDim;
+    if (tid < kHeadDim / 2u) {
+      const float x0 = a.k[kv * kHeadDim + 2u * tid], x1 = a.k[kv * kHeadDim + 2u * tid + 1u];
+      const float cs = sh.cs[tid], sn = sh.sn[tid];
+      const float r0 = x0 * cs - x1 * sn, r1 = x0 * sn + x1 * cs;
+      a.k_cache[at + 2u * tid] = __float2half_rn(r0);
+      a.k_cache[at + 2u * tid + 1u] = __float2half_rn(r1);
+    } else if (tid < kHeadDim) {
+      const uint32_t j = tid - kHeadDim / 2u;
+      a.v_cache[at + 2u * j] = __float2half_rn(a.v[kv * kHeadDim + 2u * j]);
+      a.v_cache[at + 2u * j + 1u] = __float2half_rn(a.v[kv * kHeadDim + 2u * j + 1u]);
+    }
+    __threadfence_block();
+    __syncthreads();
+  }
+  return true;
+}
+
+// q[h][2i], q[h][2i+1] rotated by the position's angle i.
+__device__ __forceinline__ float2 rope_pair(float x0, float x1, const AttnShared& sh, uint32_t i) {
+  const float cs = sh.cs[i], sn = sh.sn[i];
+  return make_float2(x0 * cs - x1 * sn, x0 * sn + x1 * cs);
 }
 
 // Partial attention of one kv head over positions [span*kSpan, min(+kSpan, ctx_len)),
@@ -84,28 +124,34 @@ cudaError_t launch_rope_append(float* q, float* k, const float* v, void* k_cache
 //           its 8 K loads in flight at once, the halves combined by one shuffle;
 //   values: thread d -> output dimension d, positions in blocks of 16 loads.
 template <uint32_t G>
-__global__ void __launch_bounds__(128) attn_split_kernel(const float* __restrict__ q,
-                                                         const __half* __restrict__ k_cache,
-                                                         const __half* __restrict__ v_cache,
-                                                         uint32_t ctx_max, uint32_t ctx_len_arg,
-                                                         const uint32_t* pos_dev, uint32_t ctx_limit,
-                                                         uint32_t spans, float* partial) {
+__global__ void __launch_bounds__(128) attn_split_kernel(const AttnStep a) {
   static_assert(kSpan * 2u == 128u, "two threads per position");
   __shared__ __align__(16) float qs[G][kHeadDim];
   __shared__ float p[G][kSpan];
   __shared__ float red[G][4];
   __shared__ float mx[G], sm[G];
+  __shared__ __align__(16) AttnShared sh;
   const uint32_t kv = blockIdx.x, span = blockIdx.y, tid = threadIdx.x;
   const uint32_t lane = tid & 31u, warp = tid >> 5;
   const uint32_t t0 = span * kSpan;
   const float scale = rsqrtf(static_cast<float>(kHeadDim));
-  pdl_wait();
-  pdl_trigger();
-  const uint32_t ctx_len = pos_dev != nullptr ? min(step_position(0u, pos_dev) + 1u, ctx_limit) : ctx_len_arg;
-  if (t0 >= ctx_len) return;  // a span of the graph's bucket beyond this token's context
+  const uint32_t ctx_max = a.ctx_max;
+  const __half* __restrict__ k_cache = a.k_cache;
+  const __half* __restrict__ v_cache = a.v_cache;
+  uint32_t ctx_len = 0, step_pos = 0;
+  bool owner = false;
+  if (!attn_prologue(a, kv, span, sh, ctx_len, step_pos, owner)) return;
   const uint32_t n = min(kSpan, ctx_len - t0);
-  for (uint32_t i = tid; i < G * kHeadDim; i += blockDim.x) {
-    qs[i / kHeadDim][i % kHeadDim] = q[(kv * G) * kHeadDim + i] * scale;
+  if (!owner) {
+    rope_table(a, step_pos, sh);
+    __syncthreads();
+  }
+  for (uint32_t i = tid; i < G * (kHeadDim / 2u); i += blockDim.x) {  // rotated, scaled q
+    const uint32_t h = i / (kHeadDim / 2u), j = i - h * (kHeadDim / 2u);
+    const float* qh = a.q + (kv * G + h) * kHeadDim;
+    const float2 r = rope_pair(qh[2u * j], qh[2u * j + 1u], sh, j);
+    qs[h][2u * j] = r.x * scale;
+    qs[h][2u * j + 1u] = r.y * scale;
   }
   __syncthreads();
   const uint32_t pos = tid >> 1, half = tid & 1u;
@@ -118,7 +164,7 @@ __global__ void __launch_bounds__(128) attn_split_kernel(const float* __restrict
         k_cache + (static_cast<size_t>(kv) * ctx_max + t0 + pos) * kHeadDim + half * 64u);
     uint4 kw[8];
 #pragma unroll
-    for (uint32_t c = 0; c < 8u; ++c) kw[c] = __ldg(kr + c);
+    for (uint32_t c = 0; c < 8u; ++c) kw[c] = __ldcg(kr + c);  // L2: the new row may be this CTA's write
 #pragma unroll
     for (uint32_t c = 0; c < 8u; ++c) {
       const __half2* hw = reinterpret_cast<const __half2*>(&kw[c]);
@@ -176,7 +222,7 @@ __global__ void __launch_bounds__(128) attn_split_kernel(const float* __restrict
   for (; t + 16u <= n; t += 16u) {
     float vv[16];
 #pragma unroll
-    for (uint32_t j = 0; j < 16u; ++j) vv[j] = __half2float(vb[static_cast<size_t>(t + j) * kHeadDim]);
+    for (uint32_t j = 0; j < 16u; ++j) vv[j] = __half2float(__ldcg(vb + static_cast<size_t>(t + j) * kHeadDim));
 #pragma unroll
     for (uint32_t j = 0; j < 16u; ++j) {
 #pragma unroll
@@ -184,15 +230,14 @@ __global__ void __launch_bounds__(128) attn_split_kernel(const float* __restrict
     }
   }
   for (; t < n; ++t) {
-    const float vv = __half2float(vb[static_cast<size_t>(t) * kHeadDim]);
+    const float vv = __half2float(__ldcg(vb + static_cast<size_t>(t) * kHeadDim));
 #pragma unroll
     for (uint32_t h = 0; h < G; ++h) o[h] = fmaf(p[h][t], vv, o[h]);
   }
   __syncthreads();
-  const uint32_t stride = kHeadDim + 2u;
 #pragma unroll
   for (uint32_t h = 0; h < G; ++h) {
-    float* dst = partial + ((static_cast<size_t>(kv * G + h) * spans) + span) * stride;
+    float* dst = a.partial + ((static_cast<size_t>(kv * G + h) * a.spans) + span) * kRec;
     dst[tid] = o[h];
     if (tid == 0u) {
       dst[kHeadDim] = mx[h];
@@ -250,27 +295,23 @@ __device__ __forceinline__ void split_half2(float x, float y, uint32_t& hi, uint
 
 constexpr uint32_t kTcGroup = 8;  // q heads per kv head the tensor-core split handles (<=)
 
-__global__ void __launch_bounds__(128) attn_split_tc_kernel(const float* __restrict__ q,
-                                                            const __half* __restrict__ k_cache,
-                                                            const __half* __restrict__ v_cache,
-                                                            uint32_t G, uint32_t ctx_max,
-                                                            uint32_t ctx_len_arg,
-                                                            const uint32_t* pos_dev,
-                                                            uint32_t ctx_limit, uint32_t spans,
-                                                            float* partial) {
+__global__ void __launch_bounds__(128) attn_split_tc_kernel(const AttnStep a) {
   static_assert(kSpan == 64u, "four warps of 16 positions");
   __shared__ __align__(128) uint8_t vs[kSpan * kHeadDim * 2u];  // the span's V, swizzled
   __shared__ float ps[4][16][9];                                 // P per warp [pos][head]
   __shared__ float ow[4][kTcGroup][kHeadDim + 4u];               // per-warp O^T [head][dim]
   __shared__ float wmax[4][kTcGroup], wsum[4][kTcGroup];
+  __shared__ __align__(16) AttnShared sh;
   const uint32_t kv = blockIdx.x, span = blockIdx.y, tid = threadIdx.x;
   const uint32_t lane = tid & 31u, warp = tid >> 5, g = lane >> 2, t = lane & 3u;
   const uint32_t t0 = span * kSpan;
   const float scale = rsqrtf(static_cast<float>(kHeadDim));
-  pdl_wait();  // q and the newest K/V row come from the previous kernel
-  pdl_trigger();
-  const uint32_t ctx_len = pos_dev != nullptr ? min(step_position(0u, pos_dev) + 1u, ctx_limit) : ctx_len_arg;
-  if (t0 >= ctx_len) return;  // a span of the graph's bucket beyond this token's context
+  const uint32_t G = a.G, ctx_max = a.ctx_max;
+  const __half* __restrict__ k_cache = a.k_cache;
+  const __half* __restrict__ v_cache = a.v_cache;
+  uint32_t ctx_len = 0, pos = 0;
+  bool owner = false;
+  if (!attn_prologue(a, kv, span, sh, ctx_len, pos, owner)) return;
   const uint32_t n = min(kSpan, ctx_len - t0);
 
   // V of the span -> shared memory (rows past the context are zero).
@@ -286,18 +327,6 @@ __global__ void __launch_bounds__(128) attn_split_tc_kernel(const float* __restr
   }
   asm volatile("cp.async.commit_group;" ::: "memory");
 
-  // B fragments of the scores: q head g, dims 32t .. 32t + 31 (scaled), as hi + lo.
-  uint32_t qh[8][2], ql[8][2];
-  {
-    const float4* qr = reinterpret_cast<const float4*>(
-        q + (static_cast<size_t>(kv) * G + g) * kHeadDim + 32u * t);
-#pragma unroll
-    for (uint32_t j = 0; j < 8u; ++j) {
-      const float4 v = g < G ? qr[j] : make_float4(0.f, 0.f, 0.f, 0.f);
-      split_half2(v.x * scale, v.y * scale, qh[j][0], ql[j][0]);
-      split_half2(v.z * scale, v.w * scale, qh[j][1], ql[j][1]);
-    }
-  }
   // A fragments: K rows r0 = 16w + g and r1 = r0 + 8, dims 32t .. 32t + 31.
   const uint32_t r0 = warp * 16u + g, r1 = r0 + 8u;
   uint4 ka[4], kb[4];
@@ -307,9 +336,29 @@ __global__ void __launch_bounds__(128) attn_split_tc_kernel(const float* __restr
     const uint4* k1 = reinterpret_cast<const uint4*>(
         k_cache + (static_cast<size_t>(kv) * ctx_max + t0 + r1) * kHeadDim + 32u * t);
 #pragma unroll
-    for (uint32_t c = 0; c < 4u; ++c) {
-      ka[c] = r0 < n ? __ldg(k0 + c) : make_uint4(0u, 0u, 0u, 0u);
-      kb[c] = r1 < n ? __ldg(k1 + c) : make_uint4(0u, 0u, 0u, 0u);
+    for (uint32_t c = 0; c < 4u; ++c) {  // L2 loads: the new row may be this CTA's write
+      ka[c] = r0 < n ? __ldcg(k0 + c) : make_uint4(0u, 0u, 0u, 0u);
+      kb[c] = r1 < n ? __ldcg(k1 + c) : make_uint4(0u, 0u, 0u, 0u);
+    }
+  }
+  // the rotation table while the span's loads are in flight (the owner built it earlier)
+  if (!owner) {
+    rope_table(a, pos, sh);
+    __syncthreads();
+  }
+  // B fragments of the scores: q head g, dims 32t .. 32t + 31 (rotated, scaled), as
+  // hi + lo.
+  uint32_t qh[8][2], ql[8][2];
+  {
+    const float4* qr = reinterpret_cast<const float4*>(
+        a.q + (static_cast<size_t>(kv) * G + g) * kHeadDim + 32u * t);
+#pragma unroll
+    for (uint32_t j = 0; j < 8u; ++j) {
+      const float4 v = g < G ? qr[j] : make_float4(0.f, 0.f, 0.f, 0.f);
+      const uint32_t i0 = 16u * t + 2u * j;  // pair index of dims (32t + 4j, +1)
+      const float2 r0 = rope_pair(v.x, v.y, sh, i0), r1 = rope_pair(v.z, v.w, sh, i0 + 1u);
+      split_half2(r0.x * scale, r0.y * scale, qh[j][0], ql[j][0]);
+      split_half2(r1.x * scale, r1.y * scale, qh[j][1], ql[j][1]);
     }
   }
   float sc[4] = {0.f, 0.f, 0.f, 0.f};
@@ -380,7 +429,7 @@ __global__ void __launch_bounds__(128) attn_split_tc_kernel(const float* __restr
   }
   __syncthreads();
   for (uint32_t h = 0; h < G; ++h) {
-    float* dst = partial + ((static_cast<size_t>(kv * G + h) * spans) + span) * (kHeadDim + 2u);
+    float* dst = a.partial + ((static_cast<size_t>(kv * G + h) * a.spans) + span) * kRec;
     dst[tid] = ((ow[0][h][tid] + ow[1][h][tid]) + ow[2][h][tid]) + ow[3][h][tid];
     if (tid == 0u) {
       dst[kHeadDim] = fmaxf(fmaxf(wmax[0][h], wmax[1][h]), fmaxf(wmax[2][h], wmax[3][h]));
@@ -396,29 +445,29 @@ __global__ void __launch_bounds__(128) attn_split_tc_kernel(const float* __restr
 constexpr uint32_t kMaxSpans = 4096;
 
 __global__ void __launch_bounds__(64) attn_combine_kernel(const float* __restrict__ partial,
-                                                          uint32_t spans, uint32_t used_arg,
+                                                          uint32_t spans, uint32_t pos_arg,
                                                           const uint32_t* pos_dev, uint32_t ctx_limit,
                                                           float* out, ActChunk* act) {
   __shared__ float wgt[kMaxSpans];
   __shared__ float red[2];
   pdl_wait();
   pdl_trigger();
-  const uint32_t used_spans =
-      pos_dev != nullptr ? (min(step_position(0u, pos_dev) + 1u, ctx_limit) + kSpan - 1u) / kSpan : used_arg;
+  const uint32_t pos = step_position(pos_arg, pos_dev);
+  if (pos >= ctx_limit) return;  // the split launch recorded QG_ERR_POSITION
+  const uint32_t used_spans = (pos + kSpan) / kSpan;
   const uint32_t h = blockIdx.x, tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
-  const uint32_t stride = kHeadDim + 2u;
-  const float* base = partial + static_cast<size_t>(h) * spans * stride;
+  const float* base = partial + static_cast<size_t>(h) * spans * kRec;
   float m = -INFINITY;
-  for (uint32_t s = tid; s < used_spans; s += 64u) m = fmaxf(m, base[s * stride + kHeadDim]);
+  for (uint32_t s = tid; s < used_spans; s += 64u) m = fmaxf(m, base[s * kRec + kHeadDim]);
   for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
   if (lane == 0u) red[warp] = m;
   __syncthreads();
   m = fmaxf(red[0], red[1]);
   float z = 0.f;
   for (uint32_t s = tid; s < used_spans; s += 64u) {
-    const float w = __expf(base[s * stride + kHeadDim] - m);
+    const float w = __expf(base[s * kRec + kHeadDim] - m);
     wgt[s] = w;
-    z = fmaf(w, base[s * stride + kHeadDim + 1u], z);
+    z = fmaf(w, base[s * kRec + kHeadDim + 1u], z);
   }
   for (int off = 16; off > 0; off >>= 1) z += __shfl_xor_sync(0xffffffffu, z, off);
   __syncthreads();  // red is reused; the weights are complete
@@ -427,7 +476,7 @@ __global__ void __launch_bounds__(64) attn_combine_kernel(const float* __restric
   z = red[0] + red[1];
   float o0 = 0.f, o1 = 0.f;
   const float2* col = reinterpret_cast<const float2*>(base) + tid;  // columns 2 tid, 2 tid + 1
-  const uint32_t stride2 = stride / 2u;
+  constexpr uint32_t stride2 = kRec / 2u;
   uint32_t s = 0;
   for (; s + 8u <= used_spans; s += 8u) {
     float2 v[8];
@@ -454,55 +503,62 @@ __global__ void __launch_bounds__(64) attn_combine_kernel(const float* __restric
 
 cudaError_t attn_partial_floats(uint32_t n_q, uint32_t ctx_max, size_t* floats) {
   const uint32_t spans = (ctx_max + kSpan - 1u) / kSpan;
-  *floats = static_cast<size_t>(n_q) * spans * (kHeadDim + 2u);
+  *floats = static_cast<size_t>(n_q) * spans * kRec;
   return cudaSuccess;
 }
 
-// ctx_len: positions [0, ctx_len) when pos_dev is null; otherwise the context is
-// [0, *pos_dev] and ctx_len is the bucket the grid is sized for (positions past it are
-// not read).
-cudaError_t launch_attention(const float* q, const void* k_cache, const void* v_cache,
-                             uint32_t n_q, uint32_t n_kv, uint32_t ctx_max, uint32_t ctx_len,
-                             const uint32_t* pos_dev, float* partial, float* out, void* act,
+// One layer's decode attention at the token position (`pos`, or *pos_dev with ctx_limit
+// the graph's context bucket): RoPE, KV append and split in one launch, then the combine.
+cudaError_t launch_attention(const float* q, const float* k, const float* v, void* k_cache,
+                             void* v_cache, uint32_t n_q, uint32_t n_kv, uint32_t ctx_max,
+                             uint32_t pos, const uint32_t* pos_dev, uint32_t ctx_limit,
+                             float rope_base, float* partial, float* out, void* act,
                              cudaStream_t stream) {
-  if (n_kv == 0u || n_q % n_kv != 0u || n_q / n_kv > kMaxGroup || ctx_len == 0u ||
-      ctx_len > ctx_max || (ctx_max + kSpan - 1u) / kSpan > kMaxSpans) {
+  if (n_kv == 0u || n_q % n_kv != 0u || n_q / n_kv > kMaxGroup ||
+      (ctx_max + kSpan - 1u) / kSpan > kMaxSpans || (pos_dev == nullptr && pos >= ctx_max)) {
     return cudaErrorInvalidValue;
   }
-  const uint32_t spans = (ctx_max + kSpan - 1u) / kSpan;
-  const uint32_t used = (ctx_len + kSpan - 1u) / kSpan;
-  const uint32_t group = n_q / n_kv;
-  const dim3 grid(n_kv, used);
-  const __half* kc = static_cast<const __half*>(k_cache);
-  const __half* vc = static_cast<const __half*>(v_cache);
-  cudaError_t e;
-  const bool tc = group <= kTcGroup && (reinterpret_cast<uintptr_t>(q) & 15u) == 0u &&
-                  (reinterpret_cast<uintptr_t>(kc) & 15u) == 0u &&
-                  (reinterpret_cast<uintptr_t>(vc) & 15u) == 0u;
+  AttnStep a{};
+  a.q = q;
+  a.k = k;
+  a.v = v;
+  a.k_cache = static_cast<__half*>(k_cache);
+  a.v_cache = static_cast<__half*>(v_cache);
+  a.partial = partial;
+  a.pos_dev = pos_dev;
+  a.G = n_q / n_kv;
+  a.ctx_max = ctx_max;
+  a.pos_arg = pos;
+  a.ctx_limit = ctx_limit < ctx_max ? ctx_limit : ctx_max;
+  a.spans = (ctx_max + kSpan - 1u) / kSpan;
+  a.rope_base = rope_base;
+  // the grid covers the context the launch may see: pos + 1, or the bucket
+  const uint32_t reach = pos_dev != nullptr ? a.ctx_limit : pos + 1u;
+  const dim3 grid(n_kv, (reach + kSpan - 1u) / kSpan);
+  const bool tc = a.G <= kTcGroup && (reinterpret_cast<uintptr_t>(q) & 15u) == 0u &&
+                  (reinterpret_cast<uintptr_t>(k_cache) & 15u) == 0u &&
+                  (reinterpret_cast<uintptr_t>(v_cache) & 15u) == 0u;
+  cudaError_t e = cudaSuccess;
   if (tc) {
-    e = launch_k(attn_split_tc_kernel, grid, 128, 0, stream, q, kc, vc, group, ctx_max, ctx_len,
-                 pos_dev, ctx_len, spans, partial);
-    if (e != cudaSuccess) return e;
-    return launch_k(attn_combine_kernel, n_q, 64, 0, stream, static_cast<const float*>(partial),
-                    spans, used, pos_dev, ctx_len, out, static_cast<ActChunk*>(act));
-  }
-  switch (group) {
-#define QG_SPLIT(G)                                                                          \
-  case G:                                                                                    \
-    e = launch_k(attn_split_kernel<G>, grid, 128, 0, stream, q, kc, vc, ctx_max, ctx_len,    \
-                 pos_dev, ctx_len, spans, partial);                                          \
+    e = launch_k(attn_split_tc_kernel, grid, 128, 0, stream, a);
+  } else {
+    switch (a.G) {
+#define QG_SPLIT(GG) \
+  case GG:           \
+    e = launch_k(attn_split_kernel<GG>, grid, 128, 0, stream, a); \
     break;
-    QG_SPLIT(1)
-    QG_SPLIT(2)
-    QG_SPLIT(4)
-    QG_SPLIT(8)
-    QG_SPLIT(16)
+      QG_SPLIT(1)
+      QG_SPLIT(2)
+      QG_SPLIT(4)
+      QG_SPLIT(8)
+      QG_SPLIT(16)
 #undef QG_SPLIT
-    default: return cudaErrorInvalidValue;
+      default: return cudaErrorInvalidValue;
+    }
   }
   if (e != cudaSuccess) return e;
-  return launch_k(attn_combine_kernel, n_q, 64, 0, stream, static_cast<const float*>(partial), spans,
-                  used, pos_dev, ctx_len, out, static_cast<ActChunk*>(act));
+  return launch_k(attn_combine_kernel, n_q, 64, 0, stream, static_cast<const float*>(partial),
+                  a.spans, pos, pos_dev, a.ctx_limit, out, static_cast<ActChunk*>(act));
 }
 
 // Local argmax of this rank's vocab shard -> (value bits, global index); lowest index

@@ -40,14 +40,13 @@
 #include "qg_host.h"
 
 namespace qg {
+// One layer's attention (qg_attn.cu): RoPE, KV append and split in one launch, then the
+// combine; `partial` holds attn_partial_floats floats of span records.
 cudaError_t attn_partial_floats(uint32_t n_q, uint32_t ctx_max, size_t* floats);
-cudaError_t launch_rope_append(float* q, float* k, const float* v, void* k_cache, void* v_cache,
-                               uint32_t n_q, uint32_t n_kv, uint32_t ctx_max, uint32_t pos,
-                               const uint32_t* pos_dev, uint32_t ctx_limit, float rope_base,
-                               cudaStream_t stream);
-cudaError_t launch_attention(const float* q, const void* k_cache, const void* v_cache,
-                             uint32_t n_q, uint32_t n_kv, uint32_t ctx_max, uint32_t ctx_len,
-                             const uint32_t* pos_dev, float* partial, float* out, void* act,
+cudaError_t launch_attention(const float* q, const float* k, const float* v, void* k_cache,
+                             void* v_cache, uint32_t n_q, uint32_t n_kv, uint32_t ctx_max,
+                             uint32_t pos, const uint32_t* pos_dev, uint32_t ctx_limit,
+                             float rope_base, float* partial, float* out, void* act,
                              cudaStream_t stream);
 cudaError_t launch_argmax_candidate(const float* v, uint32_t n, uint32_t offset, uint32_t* cand,
                                     cudaStream_t stream);
@@ -502,12 +501,9 @@ cudaError_t decoder_step(qg_decoder dec, const float* x, uint32_t pos, uint32_t*
       const uint32_t r[3] = {s.q_local, s.kv_local, s.kv_local};
       QG_TRY(qg::launch_gemv_multi(d.attn_fmt, 3, p, m, y, r, d.hidden, h, w + L.act_x, stream));
     }
-    QG_TRY(qg::launch_rope_append(q, k, v, W.k_cache, W.v_cache, s.nq_local, s.nkv_local,
-                                  d.ctx_max, pos, pos_dev, pos_dev ? ctx_bucket : d.ctx_max,
-                                  d.rope_base, stream));
-    QG_TRY(qg::launch_attention(q, W.k_cache, W.v_cache, s.nq_local, s.nkv_local, d.ctx_max,
-                                pos_dev ? ctx_bucket : pos + 1u, pos_dev, F(L.partial), attn,
-                                w + L.act_attn, stream));
+    QG_TRY(qg::launch_attention(q, k, v, W.k_cache, W.v_cache, s.nq_local, s.nkv_local, d.ctx_max,
+                                pos, pos_dev, pos_dev ? ctx_bucket : d.ctx_max, d.rope_base,
+                                F(L.partial), attn, w + L.act_attn, stream));
     QG_TRY(project_out(d.attn_fmt, W.wo, W.wo_meta, attn, w + L.act_attn, x1, cur, s.q_local,
                        dec->canon_o));
     // feed-forward block (the exchange of Wo is gathered into x1)
