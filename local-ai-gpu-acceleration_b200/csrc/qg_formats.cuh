@@ -244,17 +244,17 @@ __device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
 }
 
 // Exact int -> float for small magnitudes with full-rate ALU/FMA ops (no I2F):
-// u < 2^23 via the 2^23 magic number, |v| < 2^22 via 1.5 * 2^23.
+// u < 2^23 via the 2^23 magic number.
 __device__ __forceinline__ float u2f_small(uint32_t u) {
   return __uint_as_float(0x4b000000u | u) - 8388608.0f;
 }
-__device__ __forceinline__ float i2f_mid(int v) {
-  return __int_as_float(0x4b400000 + v) - 12582912.0f;
-}
 
-// s * (ih + il / 256)
+// s * (ih + il / 256): the two plane sums combined exactly as the integer 256 ih + il
+// (below 2^28 for every reader: |ih| <= 32 * 240 * 127), one conversion (the
+// conversion unit is otherwise idle; rounding 2^-24 relative), one multiply by s / 256
+// (a per-thread constant).
 __device__ __forceinline__ float planes_value(int ih, int il, float s) {
-  return s * fmaf(i2f_mid(il), 0.00390625f, i2f_mid(ih));
+  return __int2float_rn(ih * 256 + il) * (s * 0.00390625f);
 }
 
 // sum(q x) over both halves for 8 words of byte quants: A = lo[], B = hi[].
@@ -319,18 +319,25 @@ static_assert(kIq2Copies == 4u || kIq2Copies == 8u || kIq2Copies == 16u,
               "IQ2_S grid copies: 4, 8 or 16");
 constexpr uint32_t kIq2TableBytes = 2048u * kIq2Copies * 4u;
 
-// Byte masks of four sign bits: byte i = 0xFF where bit i of s4 (< 16) is set.  The
-// multiply puts bit i at bit 8i + 7 (its four partial products do not overlap, so no
-// carries), and prmt's sign-replicating selector copies each byte's top bit over it.
-__device__ __forceinline__ uint32_t sign_bytes4(uint32_t s4) {
-  uint32_t m;
-  asm("prmt.b32 %0, %1, 0, 0xBA98;" : "=r"(m) : "r"(s4 * 0x10204080u));
-  return m;
+// Byte masks of all eight sign bits of a byte b (< 256), with no nibble masking: lo byte i
+// = 0xFF where bit i is set, hi byte i = 0xFF where bit 4 + i is set.  b * 0x80402010
+// puts bit 3 - i at bit 8i + 7 and b * 0x08040201 puts bit 7 - i there; each multiplier's
+// four partial products of a byte cover disjoint bit ranges (4-11, 13-20, 22-29, 31-38
+// and 0-7, 9-16, 18-25, 27-34), so there are no carries and the other bits land away
+// from bit 7 of each byte; a byte-reversing sign-replicating prmt then gives the masks.
+__device__ __forceinline__ void sign_masks8(uint32_t b, uint32_t& lo, uint32_t& hi) {
+  asm("prmt.b32 %0, %1, 0, 0x89AB;" : "=r"(lo) : "r"(b * 0x80402010u));
+  asm("prmt.b32 %0, %1, 0, 0x89AB;" : "=r"(hi) : "r"(b * 0x08040201u));
 }
-// Four odd magnitudes (bytes) with the signs of s4's four bits applied (m ^ 0xFE = -m).
-__device__ __forceinline__ uint32_t apply_signs4(uint32_t mags, uint32_t s4) {
-  return mags ^ (sign_bytes4(s4) & 0xFEFEFEFEu);
+// Byte G of w, zero-extended (one prmt).
+template <int G>
+__device__ __forceinline__ uint32_t byte_at(uint32_t w) {
+  uint32_t r;
+  asm("prmt.b32 %0, %1, 0, %2;" : "=r"(r) : "r"(w), "n"(0x4440 | G));
+  return r;
 }
+// Odd magnitudes m (bytes) are negated by m ^ 0xFE (= -m in two's complement), so a
+// weight word with its signs applied is mags ^ (mask & 0xFEFEFEFE).
 // Byte g of `lo` in byte 0 and byte g of `hi` (< 128) in byte 1, zero above: the 16-bit
 // value lo_g + 256 hi_g in one prmt (the sign-replicating selector on hi's byte g, whose
 // top bit is clear, yields the zero bytes).
@@ -502,12 +509,14 @@ __device__ __forceinline__ void iq2s_sub(uint32_t gl, uint32_t sg, uint32_t qhb,
   idx[2] = pair_bytes<2>(gl, h4);
   idx[3] = pair_bytes<3>(gl, h4);
   int ih[2] = {0, 0}, il[2] = {0, 0};
+  const uint32_t sbs[4] = {byte_at<0>(sg), byte_at<1>(sg), byte_at<2>(sg), byte_at<3>(sg)};
 #pragma unroll
   for (int g = 0; g < 4; ++g) {
     const uint2 k2 = t.kgrid2[idx[g] * kIq2Copies];
-    const uint32_t sb = sg >> (8 * g);
-    const uint32_t v0 = apply_signs4(k2.x, sb & 0x0fu);
-    const uint32_t v1 = apply_signs4(k2.y, (sb >> 4) & 0x0fu);
+    uint32_t m0, m1;
+    sign_masks8(sbs[g], m0, m1);
+    const uint32_t v0 = k2.x ^ (m0 & 0xFEFEFEFEu);
+    const uint32_t v1 = k2.y ^ (m1 & 0xFEFEFEFEu);
     ih[g >> 1] = dp4a(v1, H[2 * g + 1], dp4a(v0, H[2 * g], ih[g >> 1]));
     il[g >> 1] = dp4a(v1, L[2 * g + 1], dp4a(v0, L[2 * g], il[g >> 1]));
   }
@@ -550,17 +559,18 @@ __device__ __forceinline__ void iq3s_sub(uint32_t q0, uint32_t q1, uint32_t qhb,
   idx[6] = pair_bytes<2>(q1, hb1);
   idx[7] = pair_bytes<3>(q1, hb1);
   int ih = 0, il = 0;
+  const uint32_t sbs[4] = {byte_at<0>(sg), byte_at<1>(sg), byte_at<2>(sg), byte_at<3>(sg)};
 #pragma unroll
   for (int g = 0; g < 4; ++g) {
-    const uint32_t sb = (sg >> (8 * g)) & 0xffu;
     uint32_t m0, m1;
     if constexpr (kIq3TableSigns) {
-      const uint2 sm = t.sign3[sb << 4];
+      const uint2 sm = t.sign3[sbs[g] << 4];
       m0 = sm.x;
       m1 = sm.y;
     } else {
-      m0 = sign_bytes4(sb & 0x0fu) & 0xFEFEFEFEu;
-      m1 = sign_bytes4(sb >> 4) & 0xFEFEFEFEu;
+      sign_masks8(sbs[g], m0, m1);
+      m0 &= 0xFEFEFEFEu;
+      m1 &= 0xFEFEFEFEu;
     }
     const uint32_t v0 = t.grid3[idx[2 * g] * kIq3Copies] ^ m0;
     const uint32_t v1 = t.grid3[idx[2 * g + 1] * kIq3Copies] ^ m1;

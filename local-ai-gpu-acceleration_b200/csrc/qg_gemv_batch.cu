@@ -239,12 +239,14 @@ __device__ __forceinline__ void read_sub<QG_FMT_IQ2S>(const uint8_t* rp, const u
   idx[1] = pair_bytes<1>(gl, h4);
   idx[2] = pair_bytes<2>(gl, h4);
   idx[3] = pair_bytes<3>(gl, h4);
+  const uint32_t sbs[4] = {byte_at<0>(sg), byte_at<1>(sg), byte_at<2>(sg), byte_at<3>(sg)};
 #pragma unroll
   for (int g = 0; g < 4; ++g) {
     const uint2 k2 = t.kgrid2[idx[g] * kIq2Copies];
-    const uint32_t sb = sg >> (8 * g);
-    s.w[2 * g] = apply_signs4(k2.x, sb & 0x0fu);
-    s.w[2 * g + 1] = apply_signs4(k2.y, (sb >> 4) & 0x0fu);
+    uint32_t m0, m1;
+    sign_masks8(sbs[g], m0, m1);
+    s.w[2 * g] = k2.x ^ (m0 & 0xFEFEFEFEu);
+    s.w[2 * g + 1] = k2.y ^ (m1 & 0xFEFEFEFEu);
   }
   s.s0 = static_cast<int>(2u * (scb & 0x0fu) + 1u);
   s.s1 = static_cast<int>(2u * (scb >> 4) + 1u);
@@ -270,11 +272,13 @@ __device__ __forceinline__ void read_sub<QG_FMT_IQ3S>(const uint8_t* rp, const u
   idx[5] = pair_bytes<1>(q1, hb1);
   idx[6] = pair_bytes<2>(q1, hb1);
   idx[7] = pair_bytes<3>(q1, hb1);
+  const uint32_t sbs[4] = {byte_at<0>(sg), byte_at<1>(sg), byte_at<2>(sg), byte_at<3>(sg)};
 #pragma unroll
   for (int g = 0; g < 4; ++g) {
-    const uint32_t sb = (sg >> (8 * g)) & 0xffu;
-    const uint32_t m0 = sign_bytes4(sb & 0x0fu) & 0xFEFEFEFEu;
-    const uint32_t m1 = sign_bytes4(sb >> 4) & 0xFEFEFEFEu;
+    uint32_t m0, m1;
+    sign_masks8(sbs[g], m0, m1);
+    m0 &= 0xFEFEFEFEu;
+    m1 &= 0xFEFEFEFEu;
     s.w[2 * g] = t.grid3[idx[2 * g] * kIq3Copies] ^ m0;
     s.w[2 * g + 1] = t.grid3[idx[2 * g + 1] * kIq3Copies] ^ m1;
   }
