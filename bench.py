@@ -233,9 +233,48 @@ def measure_slice(device, args) -> dict:
     stream.synchronize()
     us = e0.elapsed_time(e1) * 1e3 / n
     g.close()
-    return {"workload": "BASELINE config 3 layer slice, 8 kernels in one graph",
-            "us_per_step": us, "steps_per_s": 1e6 / us,
-            "weight_bytes": sl.weight_bytes, "GBps": sl.weight_bytes / (us * 1e-6) / 1e9}
+    res = {"workload": "BASELINE config 3 layer slice, 8 kernels in one graph",
+           "us_per_step": us, "steps_per_s": 1e6 / us,
+           "weight_bytes": sl.weight_bytes, "GBps": sl.weight_bytes / (us * 1e-6) / 1e9}
+    res["batch_buckets"] = measure_slice_buckets(sl, device, stream, args)
+    return res
+
+
+SLICE_BUCKETS = [1, 2, 4, 8, 16]
+
+
+def measure_slice_buckets(sl, device, stream, args) -> dict:
+    """The same slice for a batch of hidden vectors through one captured graph per batch
+    bucket (qg_slice_buckets_*): each run copies the batch into its bucket's rows,
+    replays that bucket's graph and copies the rows out (all inside the timed region)."""
+    import torch
+
+    from qgemv_b200.slice import SliceBuckets
+
+    sb = SliceBuckets(sl, SLICE_BUCKETS, stream)
+    cases = []
+    for batch in [1, 2, 3, 4, 8, 16]:
+        x = torch.randn(batch, sl.dims["hidden"], device=device)
+        out = torch.empty_like(x)
+        with torch.cuda.stream(stream):
+            for _ in range(max(3, args.warmup)):
+                sb.run(x, out)
+            prewarm(lambda: sb.run(x, out), stream.synchronize, seconds=0.2)
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            n = max(20, args.steps * 5)
+            e0.record(stream)
+            for _ in range(n):
+                sb.run(x, out)
+            e1.record(stream)
+        stream.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / n
+        cases.append({"batch": batch, "bucket": sb.bucket(batch), "us_per_step": round(us, 2),
+                      "rows_per_s": round(batch * 1e6 / us, 1),
+                      "weight_GBps": round(sl.weight_bytes / (us * 1e-6) / 1e9, 1)})
+    sb.close()
+    return {"buckets": SLICE_BUCKETS, "cases": cases,
+            "path": "GEMVs: batch 1 GEMV, 2-4 CUDA-core multi-vector, >= 5 tensor-core tiles"}
 
 
 REF_LAUNCHERS = {
@@ -539,6 +578,12 @@ def run_ours(args) -> int:
         if rank == 0:
             print(json.dumps({"profiling_case": args.only, "batched": stats}))
         return 0
+    if args.only == "slice":
+        # the layer slice (config 3) alone: one graph, then the batch-bucket graphs
+        stats = measure_slice(device, args)
+        if rank == 0:
+            print(json.dumps({"profiling_case": args.only, "slice": stats}))
+        return 0
     if args.only and args.only.startswith("decode:"):
         # profiling case: the decode step alone with the given number of layers
         stats = measure_decode(device, args, world, rank, layers=int(args.only.split(":")[1]))
@@ -781,7 +826,8 @@ def main() -> int:
     ap.add_argument("--only", default=None,
                     help="profiling case: run a single GEMV FMT:ROWSxCOLS (e.g. 0:32768x8192) "
                          "instead of the sweep, decode:LAYERS (the decode step alone with "
-                         "that many layers) or batched:FMT:ROWSxCOLS:BATCH (one config-4 case); "
+                         "that many layers), slice (config 3 and its batch-bucket graphs) "
+                         "or batched:FMT:ROWSxCOLS:BATCH (one config-4 case); "
                          "skips the CPU baseline")
     args = ap.parse_args()
     if args.impl == "reference":

@@ -352,6 +352,41 @@ cudaError_t qg_graph_end(cudaStream_t stream, qg_graph* out);
 cudaError_t qg_graph_launch(qg_graph graph, cudaStream_t stream);
 cudaError_t qg_graph_destroy(qg_graph graph);
 
+/* The layer slice for `batch` hidden vectors at once (x, out row-major [batch][hidden],
+ * batch 1..32): the same stages as qg_layer_slice_forward -- per-row RMSNorm (the same
+ * sum-of-squares order, so each row's h matches the single-vector slice bit for bit),
+ * Q/K/V/O, gate/up, SiLU-gate, down, residual -- with every GEMV a batched one routed
+ * like qg_gemm_batched (CUDA-core multi-vector GEMV below the tensor-core threshold,
+ * tcgen05 tiles above it for the GGUF formats); batch 1 is qg_layer_slice_forward
+ * itself.  Activations per GEMV as in
+ * qg_gemv_batched / qg_gemm_batched.  Workspace: qg_layer_slice_batched_workspace_bytes
+ * (256-B aligned); views into it: qg_layer_slice_batched_buffers ([batch][n] each). */
+cudaError_t qg_layer_slice_batched_workspace_bytes(const qg_layer_slice* s, uint32_t batch,
+                                                   size_t* bytes);
+cudaError_t qg_layer_slice_forward_batched(const qg_layer_slice* s, const float* x, float* out,
+                                           uint32_t batch, void* workspace, cudaStream_t stream);
+cudaError_t qg_layer_slice_batched_buffers(const qg_layer_slice* s, uint32_t batch, void* workspace,
+                                           qg_layer_slice_views* views);
+
+/* One captured graph per decode step and batch bucket (the reference's
+ * CudaGraphBucketDescriptor.batch_bucket, runtime/core/graphs/cuda_graph_bucket.h:16-23,
+ * whose graphs the reference never builds): qg_slice_buckets_create waits for the work
+ * pending on `stream` (any stream, the legacy default one included), then captures
+ * qg_layer_slice_forward_batched once per bucket (`batches` ascending, 1..32, at most 32
+ * buckets) on a stream of its own and returns when the graphs are uploaded; each bucket
+ * owns its padded input/output rows and workspace, allocated here.
+ * qg_slice_buckets_run(x, out, batch) uses the smallest bucket >= batch: the batch's rows
+ * are copied in, the bucket's graph replayed and the rows copied out (two device copies
+ * and one graph launch on `stream`; cudaErrorInvalidValue past the largest bucket).  Rows
+ * past `batch` never affect the live rows.  Runs of one handle must not overlap. */
+typedef struct qg_slice_buckets_s* qg_slice_buckets;
+cudaError_t qg_slice_buckets_create(const qg_layer_slice* s, const uint32_t* batches, uint32_t n,
+                                    cudaStream_t stream, qg_slice_buckets* out);
+cudaError_t qg_slice_buckets_bucket(qg_slice_buckets b, uint32_t batch, uint32_t* bucket);
+cudaError_t qg_slice_buckets_run(qg_slice_buckets b, const float* x, float* out, uint32_t batch,
+                                 cudaStream_t stream);
+cudaError_t qg_slice_buckets_destroy(qg_slice_buckets b);
+
 /* ---------------------------------------------------------------------------
  * Tensor-parallel decode step of a Llama-style mixed-quant model (
  * no reference counterpart -- the reference is single-GPU with synthetic attention).

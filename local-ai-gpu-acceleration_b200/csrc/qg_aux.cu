@@ -1,6 +1,7 @@
 // qg_aux.cu -- the small kernels around the GEMV: token argmax, the reference's
 // RMSNorm/SiLU feedback kernels, bit-exact dequantization, and the layer-slice
 // normalisation / gate kernels.
+#include <algorithm>
 #include <mutex>
 
 #include <cooperative_groups.h>
@@ -432,6 +433,73 @@ cudaError_t launch_norm_prepare(const float* x, const float* w, uint32_t n, floa
   const uint32_t chunks = n / 64u, per = kNormThreads / 32u;
   return launch_k(norm_prepare_kernel, (chunks + per - 1u) / per, kNormThreads, 0, stream, x, w, n,
                   eps, h, static_cast<ActChunk*>(act));
+}
+
+// Batched forms for the batched layer slice (row r of every [rows][n] operand).
+// norm_rows_kernel: h[r] = rmsnorm(x[r]) * w with norm_prepare_kernel's sum-of-squares
+// order, so each row holds the bits the single-vector kernel produces; grid (blocks, rows).
+__global__ void __launch_bounds__(kNormThreads) norm_rows_kernel(const float* __restrict__ x,
+                                                                 const float* __restrict__ w,
+                                                                 uint32_t n, float eps, float* h) {
+  __shared__ float ws[kNormThreads / 32u];
+  pdl_wait();
+  pdl_trigger();
+  const float* xr = x + static_cast<size_t>(blockIdx.y) * n;
+  float* hr = h + static_cast<size_t>(blockIdx.y) * n;
+  float total;
+  if ((reinterpret_cast<uintptr_t>(xr) & 15u) == 0u) {
+    const float4* x4 = reinterpret_cast<const float4*>(xr);
+    total = canon_sumsq(n / 4u, ws, [&](uint32_t j) { return x4[j]; });
+  } else {
+    total = canon_sumsq(n / 4u, ws, [&](uint32_t j) {
+      return make_float4(xr[4u * j], xr[4u * j + 1u], xr[4u * j + 2u], xr[4u * j + 3u]);
+    });
+  }
+  const float inv = 1.0f / sqrtf(total / static_cast<float>(n) + eps);
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    hr[i] = xr[i] * inv * w[i];
+  }
+}
+
+cudaError_t launch_norm_rows(const float* x, const float* w, uint32_t n, float eps, float* h,
+                             uint32_t rows, cudaStream_t stream) {
+  if (n == 0u || n % 64u != 0u || rows == 0u) return cudaErrorInvalidValue;
+  const uint32_t blocks = (n + kNormThreads * 4u - 1u) / (kNormThreads * 4u);
+  return launch_k(norm_rows_kernel, dim3(blocks, rows), kNormThreads, 0, stream, x, w, n, eps, h);
+}
+
+// a = silu(gate) * up over `total` elements.
+__global__ void silu_gate_rows_kernel(const float* __restrict__ gate, const float* __restrict__ up,
+                                      size_t total, float* a) {
+  pdl_wait();
+  pdl_trigger();
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    a[i] = silu(gate[i]) * up[i];
+  }
+}
+
+cudaError_t launch_silu_gate_rows(const float* gate, const float* up, size_t total, float* a,
+                                  cudaStream_t stream) {
+  const uint32_t blocks = static_cast<uint32_t>(std::min<size_t>((total + 255u) / 256u, 4096u));
+  return launch_k(silu_gate_rows_kernel, blocks, 256, 0, stream, gate, up, total, a);
+}
+
+// out = x + y over `total` elements (the batched slice's residual).
+__global__ void add_rows_kernel(const float* __restrict__ x, const float* __restrict__ y,
+                                size_t total, float* out) {
+  pdl_wait();
+  pdl_trigger();
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    out[i] = x[i] + y[i];
+  }
+}
+
+cudaError_t launch_add_rows(const float* x, const float* y, size_t total, float* out,
+                            cudaStream_t stream) {
+  const uint32_t blocks = static_cast<uint32_t>(std::min<size_t>((total + 255u) / 256u, 4096u));
+  return launch_k(add_rows_kernel, blocks, 256, 0, stream, x, y, total, out);
 }
 
 // a = silu(gate) * up fused with a's activation preparation (one warp per 64 columns;

@@ -1181,6 +1181,26 @@ cudaError_t launch_gemm_tc(int fmt, const uint8_t* payload, const float* x, floa
 
 bool gemm_tc_supports(int fmt) { return tc_format(fmt); }
 
+bool batched_uses_tc(int fmt, const uint8_t* payload, uint32_t batch) {
+  return batch >= tc_min_batch() && tc_format(fmt) && (reinterpret_cast<uintptr_t>(payload) & 15u) == 0u;
+}
+
+size_t batched_gemm_ws_bytes(int fmt, uint32_t batch, uint32_t rows, uint32_t cols) {
+  if (batch < tc_min_batch() || !tc_format(fmt)) return 0u;
+  size_t bytes = 0;
+  gemm_tc_workspace_bytes(batch, rows, cols, &bytes);
+  return bytes;
+}
+
+cudaError_t launch_batched_gemm(int fmt, const uint8_t* payload, const uint8_t* meta, const float* x,
+                                float* y, uint32_t batch, uint32_t rows, uint32_t cols,
+                                void* workspace, cudaStream_t stream) {
+  if (workspace != nullptr && batched_uses_tc(fmt, payload, batch)) {
+    return launch_gemm_tc(fmt, payload, x, y, batch, rows, cols, workspace, stream);
+  }
+  return launch_gemv_vectors(fmt, payload, meta, x, y, batch, rows, cols, stream);
+}
+
 // First batch size qg_gemm_batched runs on the tensor cores: kTcMinBatch, or the
 // QG_TC_MIN_BATCH environment variable (2..33; 33 keeps every batch on the CUDA cores),
 // read once per process.

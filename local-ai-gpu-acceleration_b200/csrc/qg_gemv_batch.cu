@@ -1,5 +1,6 @@
 // qg_gemv_batch.cu -- multi-vector quantized GEMV on the CUDA cores: the batched decode
-// path below batch 16 (the tensor cores take batch >= 16, qg_gemm_tc.cu).  No reference
+// path below the tensor-core threshold (qg_gemm_tc.cu takes batch >= 5, the crossover
+// measured on B200) and every batch of qg_gemv_batched.  No reference
 // counterpart: every reference matvec kernel is batch 1
 // (runtime/kernels/decode/decode_kernels.cu).
 //
@@ -26,16 +27,18 @@
 //
 // Work.  Lane l of warp w owns sub-block 32 w + l of the slice (its x values live in
 // registers for the whole launch: 16 words per vector).  Persistent CTAs take units of
-// q consecutive rows; thread 0 streams each unit's row slices (one 1-D bulk copy per
-// row and array, the 16-B aligned window around the slice, L2 evict-first) into a ring
-// of shared-memory stages, refilling a stage after the per-unit barrier that shows every
-// warp has read it (no producer warp: at 8 warps a CTA keeps two per SM sub-partition,
-// which leaves each thread the 255 registers the 8-vector form needs).  Per row a lane
-// decodes its 32 weights into eight byte words, runs 16 dp2a per vector, scales, and the
-// warp sums the NV values with a transposed butterfly; warps' sums meet in shared
-// memory, are added in warp order, scaled by the slice's x scale and written (slices
-// after the first add to y: slice launches are chained on the stream).  Every mbarrier
-// wait is bounded (QG_ERR_WAIT_TIMEOUT in the error word).
+// q consecutive rows; warp 0 issues the first stages' copies (lane r: row r's slices,
+// one 1-D bulk copy per row and array, the 16-B aligned window around the slice, L2
+// evict-first) into a ring of shared-memory stages.  Per row a lane decodes its 32
+// weights into eight byte words and runs 16 dp2a per vector; R = 32 / NV (at most 8)
+// rows share one transposed shuffle tree; each warp posts its partial sums of a unit to a
+// shared slot and arrives on that slot's mbarrier.  Unit j's epilogue -- the warps' sums
+// added in warp order, scaled by the slice's x scale and written (slices after the first
+// add to y: slice launches are chained on the stream), and the refill of its stage with
+// unit j + S -- is done by warp j % W after its own part of unit j + 1, so no CTA-wide
+// barrier stalls the warps (no producer warp either: at 8 warps a CTA keeps two per SM
+// sub-partition, which leaves each thread the 255 registers the 8-vector form needs).
+// Every mbarrier wait is bounded (QG_ERR_WAIT_TIMEOUT in the error word).
 #include <algorithm>
 #include <map>
 #include <mutex>

@@ -91,6 +91,22 @@ cudaError_t launch_gemv_vectors(int fmt, const uint8_t* payload, const uint8_t* 
                                 float* y, uint32_t batch, uint32_t rows, uint32_t cols,
                                 cudaStream_t stream);
 
+// Batched-slice helpers (row r of every [rows][n] operand): h[r] = rmsnorm(x[r]) * w
+// (norm_prepare's sum-of-squares order), a = silu(gate) * up, out = x + y.
+cudaError_t launch_norm_rows(const float* x, const float* w, uint32_t n, float eps, float* h,
+                             uint32_t rows, cudaStream_t stream);
+cudaError_t launch_silu_gate_rows(const float* gate, const float* up, size_t total, float* a,
+                                  cudaStream_t stream);
+cudaError_t launch_add_rows(const float* x, const float* y, size_t total, float* out,
+                            cudaStream_t stream);
+// Y = W X for `batch` vectors with qg_gemm_batched's routing (batch-1 GEMV, CUDA-core
+// multi-vector GEMV below the tensor-core threshold, tensor-core tiles above for the
+// four GGUF formats); batched_gemm_ws_bytes is the tensor-core workspace it needs.
+size_t batched_gemm_ws_bytes(int fmt, uint32_t batch, uint32_t rows, uint32_t cols);
+cudaError_t launch_batched_gemm(int fmt, const uint8_t* payload, const uint8_t* meta, const float* x,
+                                float* y, uint32_t batch, uint32_t rows, uint32_t cols,
+                                void* workspace, cudaStream_t stream);
+
 // Bytes of a prepared activation of `cols` values (176 per 64 columns).
 inline size_t act_bytes(uint32_t cols) { return static_cast<size_t>(cols / 64u) * 176u; }
 cudaError_t launch_act_prepare(const float* x, uint32_t cols, void* act, cudaStream_t stream);

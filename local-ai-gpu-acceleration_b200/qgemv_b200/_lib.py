@@ -68,6 +68,13 @@ SIGNATURES: dict[str, list] = {
     "qg_gemm_batched": [c_int, P, P, P, P, U32, U32, U32, P, P],
     "qg_layer_slice_forward": [P, P, P, P, P],
     "qg_layer_slice_forward_static": [P, P, P, P],
+    "qg_layer_slice_batched_workspace_bytes": [P, U32, P],
+    "qg_layer_slice_forward_batched": [P, P, P, U32, P, P],
+    "qg_layer_slice_batched_buffers": [P, U32, P, P],
+    "qg_slice_buckets_create": [P, P, U32, P, P],
+    "qg_slice_buckets_bucket": [P, U32, P],
+    "qg_slice_buckets_run": [P, P, P, U32, P],
+    "qg_slice_buckets_destroy": [P],
     "qg_graph_begin": [P],
     "qg_graph_end": [P, P],
     "qg_graph_launch": [P, P],

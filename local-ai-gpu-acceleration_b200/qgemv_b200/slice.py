@@ -86,6 +86,44 @@ class LayerSlice:
               self.workspace.data_ptr(), s)
         return out
 
+    def batched_workspace(self, batch: int) -> torch.Tensor:
+        n = ctypes.c_size_t(0)
+        check("qg_layer_slice_batched_workspace_bytes", ctypes.byref(self.c), batch, ctypes.byref(n))
+        return torch.empty(n.value, dtype=torch.uint8, device=self.device)
+
+    def forward_batched(self, x: torch.Tensor, out: torch.Tensor | None = None,
+                        workspace: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+        """x: [batch, hidden] fp32 -> [batch, hidden] (qg_layer_slice_forward_batched)."""
+        batch = x.shape[0]
+        if out is None:
+            out = torch.empty_like(x)
+        if workspace is None:
+            workspace = self.batched_workspace(batch)
+        self._batched_ws = workspace
+        s = (stream or torch.cuda.current_stream()).cuda_stream
+        check("qg_layer_slice_forward_batched", ctypes.byref(self.c), x.data_ptr(), out.data_ptr(), batch,
+              workspace.data_ptr(), s)
+        return out
+
+    def batched_views(self, batch: int, workspace: torch.Tensor | None = None) -> dict[str, torch.Tensor]:
+        """[batch, n] views of the intermediates of the last forward_batched."""
+        ws = workspace if workspace is not None else self._batched_ws
+        v = LayerSliceViews()
+        check("qg_layer_slice_batched_buffers", ctypes.byref(self.c), batch, ws.data_ptr(), ctypes.byref(v))
+        return self._views_of(v, ws, batch)
+
+    def _views_of(self, v, ws, batch):
+        d = self.dims
+        sizes = dict(h=d["hidden"], q=d["q_rows"], k=d["kv_rows"], v=d["kv_rows"], o=d["hidden"],
+                     gate=d["ffn"], up=d["ffn"], act=d["ffn"])
+        out = {}
+        base = ws.data_ptr()
+        for name, size in sizes.items():
+            off = getattr(v, name) - base
+            t = ws[off : off + 4 * size * batch].view(torch.float32)
+            out[name] = t if batch == 0 else t.view(batch, size)
+        return out
+
     def views(self) -> dict[str, torch.Tensor]:
         v = LayerSliceViews()
         check("qg_layer_slice_buffers", ctypes.byref(self.c), self.workspace.data_ptr(), ctypes.byref(v))
@@ -98,6 +136,41 @@ class LayerSlice:
             off = getattr(v, name) - base
             out[name] = self.workspace[off : off + 4 * size].view(torch.float32)
         return out
+
+
+class SliceBuckets:
+    """One captured graph per batch bucket of the batched slice (qg_slice_buckets_*)."""
+
+    def __init__(self, sl: LayerSlice, batches, stream: torch.cuda.Stream | None = None):
+        self.slice = sl  # keeps the weights alive
+        self.stream = stream or torch.cuda.current_stream(sl.device)
+        arr = (ctypes.c_uint32 * len(batches))(*batches)
+        self.handle = c_void_p(None)
+        check("qg_slice_buckets_create", ctypes.byref(sl.c), arr, len(batches), self.stream.cuda_stream,
+              ctypes.byref(self.handle))
+
+    def bucket(self, batch: int) -> int:
+        b = ctypes.c_uint32(0)
+        check("qg_slice_buckets_bucket", self.handle, batch, ctypes.byref(b))
+        return b.value
+
+    def run(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        if out is None:
+            out = torch.empty_like(x)
+        check("qg_slice_buckets_run", self.handle, x.data_ptr(), out.data_ptr(), x.shape[0],
+              self.stream.cuda_stream)
+        return out
+
+    def close(self) -> None:
+        if self.handle.value:
+            check("qg_slice_buckets_destroy", self.handle)
+            self.handle = c_void_p(None)
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 class StepGraph:
