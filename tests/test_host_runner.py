@@ -68,6 +68,42 @@ def test_admission_rejects_every_rank_when_one_is_over_budget(host, tmp_path, tp
             assert j["over_budget_bytes"] > 0 and j["required_bytes"] > j["usable_bytes"]
 
 
+def _reference_harness():
+    """The reference's own bench harness module (tools/bench/native_harness.py), loaded
+    from the reference tree when it is present."""
+    import importlib.util
+    import sys
+
+    sys.path.insert(0, str(REPO / "oracle"))
+    import qoracle
+
+    path = qoracle.REFERENCE_ROOT / "tools" / "bench" / "native_harness.py"
+    if not path.exists():
+        pytest.skip("reference tree not present")
+    spec = importlib.util.spec_from_file_location("native_harness", path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def test_reference_harness_reads_the_runner(host, tmp_path):
+    """The bench-harness contract through the reference's own harness code: run_command
+    parses the runner's one JSON object and keeps its exit code (0 admitted, 2 rejected),
+    and write_metric_artifact turns it into a harness row."""
+    harness = _reference_harness()
+    ok = harness.run_command([str(host), "--tp", "1", "--rank", "0", "--rendezvous", str(tmp_path / "a"),
+                              "--admission-only", "--vram-free-bytes", "180000000000"], timeout=120)
+    assert ok["returncode"] == 0 and "parse_error" not in ok
+    assert ok["metrics"]["admitted"] is True and ok["metrics"]["required_bytes"] > 0
+    bad = harness.run_command([str(host), "--tp", "1", "--rank", "0", "--rendezvous", str(tmp_path / "b"),
+                               "--admission-only", "--vram-free-bytes", "5000000000"], timeout=120)
+    assert bad["returncode"] == 2 and bad["metrics"]["admitted"] is False
+    ok["name"] = "tp_decode_host"
+    art = harness.write_metric_artifact(tmp_path, ok, stamp=1, generated_at="now")
+    row = json.loads(art.read_text())
+    assert row["returncode"] == 0 and row["admitted"] is True and row["command"][0] == str(host)
+
+
 def test_admission_admits_within_budget(host, tmp_path):
     res = _ranks(host, 2, tmp_path, lambda r: ["--admission-only", "--vram-free-bytes", 180_000_000_000])
     for rc, so, se in res:
