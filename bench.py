@@ -59,8 +59,10 @@ CONFIG = {
     "entry_point": "qg_act_prepare once per distinct x + qg_gemv_act per GEMV (C-ABI), one CUDA graph per step",
     "activation_precision": "fp32 x quantized per 32 columns into two int8 planes "
                             "(x ~= s*(hi + lo/256), |error| <= 3.2e-5*||x||_inf per element) for "
-                            "the batch-1 GEMVs; fp16 (power-of-two scaled per row) on the tcgen05 "
-                            "batched path; fp32 accumulation and fp32 outputs",
+                            "the batch-1 GEMVs; int16 per (vector, column slice) on the CUDA-core "
+                            "multi-vector path (batch 2-4, |error| <= 1.6e-5*||x||_inf); fp16 "
+                            "(power-of-two scaled per row) on the tcgen05 batched path (batch >= 5); "
+                            "fp32 accumulation and fp32 outputs",
 }
 
 
@@ -530,7 +532,7 @@ def measure_decode(device, args, world: int, rank: int, layers: int | None = Non
     res.update({"ms_per_token": fused["ms_per_token"], "tok_per_s": fused["tok_per_s"],
                 "token": fused["token"], "GBps_aggregate": moved / (fused["ms_per_token"] * 1e-3) / 1e9,
                 "weight_bytes": spec.weight_bytes(), "kv_bytes": spec.kv_bytes_read(spec.ctx_max),
-                "launches_per_token": spec.layers * 10 + 4})
+                "launches_per_token": spec.layers * 9 + 4})
     if world > 1:
         nccl = timed(w, world, rank, decoder.COLLECTIVE_NCCL, True)
         dist.barrier()
