@@ -296,16 +296,19 @@ __global__ void __launch_bounds__(256) gemv_rowwise_kernel(const GemvArgs a) {
 // Tiled kernel: the production path for 16-B aligned packs.
 
 // Issue the TMA for stage `s` holding rows [row_begin, row_begin + stage_rows) of the
-// pack (fewer at its end).  The last stage of a pack may end off a 16-B boundary:
-// its tail bytes are copied here, before the arrive that publishes the stage.
+// pack, fewer at the end of the tile (row_end: a tile may end inside a stage) or of the
+// pack.  A stage may end off a 16-B boundary: its tail bytes are copied here, before the
+// arrive that publishes the stage.
 template <int FMT>
 __device__ __forceinline__ void tiled_issue(const GemvArgs& a, const GemvSeg& g, uint8_t* st,
-                                            uint64_t* bar, uint32_t row_begin, uint64_t policy) {
+                                            uint64_t* bar, uint32_t row_begin, uint32_t row_end,
+                                            uint64_t policy) {
   constexpr uint32_t PB = FmtTraits<FMT>::payload_bytes;
   constexpr uint32_t MB = FmtTraits<FMT>::meta_bytes;
   const uint32_t bpr = a.cols >> 8;
+  const uint32_t limit = min(g.rows, row_end);
   uint32_t nr = 0u;
-  if (row_begin < g.rows) nr = min(a.stage_rows, g.rows - row_begin);
+  if (row_begin < limit) nr = min(a.stage_rows, limit - row_begin);
   const uint32_t pb = nr * bpr * PB, mb = nr * bpr * MB;
   const uint32_t pb16 = pb & ~15u, mb16 = mb & ~15u;
   const uint8_t* src = g.payload + static_cast<uint64_t>(row_begin) * bpr * PB;
@@ -405,7 +408,8 @@ __global__ void __launch_bounds__(544, 1) gemv_tiled_kernel(const GemvArgs a) {
   const uint32_t nconsumers = blockDim.x - 32u;  // the last warp is the producer
   const uint32_t first = blockIdx.x, stride = gridDim.x;
   const uint32_t n_my = a.num_tiles > first ? (a.num_tiles - first + stride - 1u) / stride : 0u;
-  const uint32_t loads_per_tile = a.passes >> a.stage_shift;
+  // a tile is passes rows-passes; its last stage may be partial
+  const uint32_t loads_per_tile = (a.passes + a.stage_mask) >> a.stage_shift;
   const uint32_t S = a.stages;
 
   uint64_t* table_bar = full + 16;
@@ -441,7 +445,7 @@ __global__ void __launch_bounds__(544, 1) gemv_tiled_kernel(const GemvArgs a) {
             if (!ok) break;
           }
           tiled_issue<FMT>(a, g, stages + s * a.stage_bytes, &full[s], row0 + j * a.stage_rows,
-                           policy);
+                           row0 + a.rows_per_tile, policy);
           ++issued;
           if (++s == S) {
             s = 0;
@@ -819,30 +823,51 @@ uint32_t ctas_per_sm(const GemvPlan& p) {
 // Passes per tile.  Tiles go round-robin to the G = min(T, slots) persistent CTAs, so
 // CTA j runs ceil(T / G) or one fewer tiles, and an SM runs whichever m CTAs the block
 // scheduler put on it (m = CTAs per SM when G exceeds the SM count, else 1).  Cost of
-// a tile size P (a multiple of the stage's q passes, at most p_max): the tiles of the m
-// busiest CTAs times (P + 1/2) -- the half pass stands for a tile's barrier and
-// epilogue -- divided by 0.6 when a CTA sized to share its SM runs alone (measured on
-// B200: one 9-warp CTA streams ~0.6 of what two do).  Ties go to the larger P.
-uint32_t balanced_passes(uint32_t total_passes, uint32_t q, uint32_t sms, uint32_t cps,
-                         uint32_t p_max) {
+// a tile size P (a multiple of the stage's q passes, or of q_align, the fewest passes
+// whose bytes are 16-B aligned, when a tile may end inside a stage; at most p_max): the
+// tiles of the m busiest CTAs times (P + 1/2) -- the half pass stands for a tile's
+// barrier and epilogue -- divided by 0.6 when a CTA sized to share its SM runs alone
+// (measured on B200: one 9-warp CTA streams ~0.6 of what two do).  Ties go to the
+// larger P.
+double tile_cost(uint32_t total_passes, uint32_t P, uint32_t sms, uint32_t cps) {
   const uint32_t slots = sms * cps;
-  uint32_t best_p = q;
-  double best_cost = 1e300;
-  for (uint32_t P = q; P <= std::max(q, p_max); P += q) {
-    const uint32_t T = (total_passes + P - 1u) / P;
-    const uint32_t G = std::min(T, slots);
-    const uint32_t k = (T + G - 1u) / G;         // tiles of the busiest CTAs
-    const uint32_t n_k = T - (k - 1u) * G;        // CTAs with k tiles
-    const uint32_t m = G > sms ? cps : 1u;        // CTAs sharing the busiest SM
-    const uint32_t tiles = n_k >= m ? m * k : n_k * k + (m - n_k) * (k - 1u);
-    double cost = static_cast<double>(tiles) * (2.0 * P + 1.0);
-    if (cps > 1u && G <= sms) cost /= 0.6;
+  const uint32_t T = (total_passes + P - 1u) / P;
+  const uint32_t G = std::min(T, slots);
+  const uint32_t k = (T + G - 1u) / G;         // tiles of the busiest CTAs
+  const uint32_t n_k = T - (k - 1u) * G;        // CTAs with k tiles
+  const uint32_t m = G > sms ? cps : 1u;        // CTAs sharing the busiest SM
+  const uint32_t tiles = n_k >= m ? m * k : n_k * k + (m - n_k) * (k - 1u);
+  double cost = static_cast<double>(tiles) * (2.0 * P + 1.0);
+  if (cps > 1u && G <= sms) cost /= 0.6;
+  return cost;
+}
+
+// Best P in steps of `step` (ties to the larger P).
+uint32_t best_passes(uint32_t total_passes, uint32_t step, uint32_t sms, uint32_t cps,
+                     uint32_t p_max, double& best_cost) {
+  uint32_t best_p = step;
+  best_cost = 1e300;
+  for (uint32_t P = step; P <= std::max(step, p_max); P += step) {
+    const double cost = tile_cost(total_passes, P, sms, cps);
     if (cost <= best_cost) {
       best_cost = cost;
       best_p = P;
     }
   }
   return best_p;
+}
+
+// Tiles are whole stages (q passes) unless tiles that end inside a stage (multiples of
+// q_align) balance at least 3% better -- the medium matrices whose rows do not spread
+// over the SMs in whole stages (e.g. 10240 x 8192: 20-pass tiles on 128 CTAs against
+// 18-pass tiles on 143).
+uint32_t balanced_passes(uint32_t total_passes, uint32_t q, uint32_t q_align, uint32_t sms,
+                         uint32_t cps, uint32_t p_max) {
+  double whole = 0.0, fine = 0.0;
+  const uint32_t pw = best_passes(total_passes, q, sms, cps, std::max(q, p_max - p_max % q), whole);
+  const uint32_t pf = best_passes(total_passes, q_align, sms, cps,
+                                  std::max(q_align, p_max - p_max % q_align), fine);
+  return fine < 0.97 * whole ? pf : pw;
 }
 
 }  // namespace
@@ -903,8 +928,8 @@ GemvPlan plan_gemv(int fmt, uint32_t rows, uint32_t cols, int sms, uint32_t grou
   p.rows_per_tile = q * p.rpp;
   plan_smem(fmt, tpr, p);
   const uint32_t cps = ctas_per_sm(p);
-  const uint32_t P = balanced_passes(total_passes, q, static_cast<uint32_t>(sms), cps,
-                                     std::max(q, p_max - p_max % q));
+  const uint32_t P = balanced_passes(total_passes, q, q_align, static_cast<uint32_t>(sms), cps,
+                                     std::max(q, p_max));
   p.passes = P;
   p.rows_per_tile = P * p.rpp;
   p.num_tiles = (rows + p.rows_per_tile - 1u) / p.rows_per_tile;
