@@ -24,6 +24,9 @@
 //    spread over the banks; IQ2_S sign masks computed in registers (qg_formats.cuh).
 //  * Every mbarrier wait is bounded (QG_ERR_WAIT_TIMEOUT); the producer waits for its
 //    copies in flight before it exits.
+//  * Two builds per format: 544 threads (96 registers per thread) and, for K-quant plans
+//    of at most 480 threads at one CTA per SM, 480 threads (128 registers: the K-quant
+//    readers spill at 96).
 // gemv_staged_kernel<FMT> handles packs whose base address is not 16-B aligned
 // (all threads copy each tile); gemv_rowwise_kernel<FMT> decodes value by value for
 // rows wider than 32768 columns.
@@ -394,8 +397,8 @@ __device__ __forceinline__ float row_total(const float* p, uint32_t gpr, uint32_
 // CANON: row sums in the canonical segment order (row_total) with lane groups of
 // a.group chunks; otherwise lane groups of 32 chunks reduce with the transposed
 // butterflies (red = 4 or 2) and narrower groups with group_sum.
-template <int FMT, bool CANON>
-__global__ void __launch_bounds__(544, 1) gemv_tiled_kernel(const GemvArgs a) {
+template <int FMT, bool CANON, uint32_t MAXT>
+__global__ void __launch_bounds__(MAXT, 1) gemv_tiled_kernel(const GemvArgs a) {
   constexpr uint32_t PB = FmtTraits<FMT>::payload_bytes;
   constexpr uint32_t MB = FmtTraits<FMT>::meta_bytes;
   extern __shared__ __align__(128) uint8_t smem[];
@@ -657,6 +660,20 @@ uint32_t resident_ctas(K kernel, uint32_t threads, uint32_t smem) {
   return static_cast<uint32_t>(n);
 }
 
+uint32_t ctas_per_sm(const GemvPlan& p);
+
+// The build of the tiled kernel for a plan.  Registers are allocated per SM
+// sub-partition (16384 each), so the 17-warp build (544 threads) leaves 96 per thread, at
+// which the K-quant readers spill; K-quant plans of at most 480 threads that run one CTA
+// per SM take the 15-warp build (128 registers per thread).  IQ plans always use 544.
+template <int FMT, bool CANON>
+void (*tiled_kernel_for(const GemvPlan& plan))(const GemvArgs) {
+  if constexpr (iq_table_bytes(FMT) == 0u) {
+    if (plan.threads <= 480u && ctas_per_sm(plan) == 1u) return gemv_tiled_kernel<FMT, CANON, 480u>;
+  }
+  return gemv_tiled_kernel<FMT, CANON, 544u>;
+}
+
 void fill_args(GemvArgs& a, const GemvPlan& plan, bool canon = false) {
   a.group = plan.group;
   a.rpp = plan.rpp;
@@ -696,11 +713,12 @@ cudaError_t launch_gemv_fmt(GemvArgs a, cudaStream_t stream) {
       a.tma_ok = 1u;
       a.nseg = 1u;
       a.seg[0] = GemvSeg{a.payload, a.meta, a.y, a.rows, plan.num_tiles};
-      const cudaError_t e = ensure_smem_attr(gemv_tiled_kernel<FMT, false>, dev.max_smem_optin);
+      const auto kernel = tiled_kernel_for<FMT, false>(plan);
+      const cudaError_t e = ensure_smem_attr(kernel, dev.max_smem_optin);
       if (e != cudaSuccess) return e;
-      const uint32_t per_sm = resident_ctas(gemv_tiled_kernel<FMT, false>, plan.threads, plan.smem_bytes);
+      const uint32_t per_sm = resident_ctas(kernel, plan.threads, plan.smem_bytes);
       const uint32_t grid = std::max(1u, std::min(plan.num_tiles, per_sm * dev.sms));
-      return launch_k(gemv_tiled_kernel<FMT, false>, grid, plan.threads, plan.smem_bytes, stream, a);
+      return launch_k(kernel, grid, plan.threads, plan.smem_bytes, stream, a);
     }
   }
   // Unaligned packs (or shapes the tiled plan cannot stage): all-thread copies.
@@ -761,11 +779,12 @@ cudaError_t launch_multi_fmt(GemvArgs a, uint32_t nseg, const GemvSeg* segs, cud
   a.meta = segs[0].meta;
   a.y = segs[0].y;
   a.rows = segs[0].rows;
-  const cudaError_t e = ensure_smem_attr(gemv_tiled_kernel<FMT, false>, dev.max_smem_optin);
+  const auto kernel = tiled_kernel_for<FMT, false>(plan);
+  const cudaError_t e = ensure_smem_attr(kernel, dev.max_smem_optin);
   if (e != cudaSuccess) return e;
-  const uint32_t per_sm = resident_ctas(gemv_tiled_kernel<FMT, false>, plan.threads, plan.smem_bytes);
+  const uint32_t per_sm = resident_ctas(kernel, plan.threads, plan.smem_bytes);
   const uint32_t grid = std::max(1u, std::min(tiles, per_sm * dev.sms));
-  return launch_k(gemv_tiled_kernel<FMT, false>, grid, plan.threads, plan.smem_bytes, stream, a);
+  return launch_k(kernel, grid, plan.threads, plan.smem_bytes, stream, a);
 }
 
 // Threads per CTA: rows-per-pass is the smallest multiple of 32/group (whole warps)
@@ -1023,11 +1042,12 @@ cudaError_t launch_canon_fmt(GemvArgs a, const GemvCanon& canon, cudaStream_t st
   a.seg[0] = GemvSeg{a.payload, a.meta, a.y, a.rows, plan.num_tiles};
   a.canon_spg = canon.seg_chunks / cg;
   a.canon_nseg = canon.nseg;
-  const cudaError_t e = ensure_smem_attr(gemv_tiled_kernel<FMT, true>, dev.max_smem_optin);
+  const auto kernel = tiled_kernel_for<FMT, true>(plan);
+  const cudaError_t e = ensure_smem_attr(kernel, dev.max_smem_optin);
   if (e != cudaSuccess) return e;
-  const uint32_t per_sm = resident_ctas(gemv_tiled_kernel<FMT, true>, plan.threads, plan.smem_bytes);
+  const uint32_t per_sm = resident_ctas(kernel, plan.threads, plan.smem_bytes);
   const uint32_t grid = std::max(1u, std::min(plan.num_tiles, per_sm * dev.sms));
-  return launch_k(gemv_tiled_kernel<FMT, true>, grid, plan.threads, plan.smem_bytes, stream, a);
+  return launch_k(kernel, grid, plan.threads, plan.smem_bytes, stream, a);
 }
 
 cudaError_t launch_canon(int fmt, const GemvArgs& a, const GemvCanon& canon, cudaStream_t stream) {
