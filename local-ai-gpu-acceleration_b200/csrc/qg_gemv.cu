@@ -877,7 +877,7 @@ uint32_t best_passes(uint32_t total_passes, uint32_t step, uint32_t sms, uint32_
 }
 
 // Tiles are whole stages (q passes) unless tiles that end inside a stage (multiples of
-// q_align) balance at least 3% better -- the medium matrices whose rows do not spread
+// q_align) balance at least 2% better -- the medium matrices whose rows do not spread
 // over the SMs in whole stages (e.g. 10240 x 8192: 20-pass tiles on 128 CTAs against
 // 18-pass tiles on 143).
 uint32_t balanced_passes(uint32_t total_passes, uint32_t q, uint32_t q_align, uint32_t sms,
@@ -886,7 +886,7 @@ uint32_t balanced_passes(uint32_t total_passes, uint32_t q, uint32_t q_align, ui
   const uint32_t pw = best_passes(total_passes, q, sms, cps, std::max(q, p_max - p_max % q), whole);
   const uint32_t pf = best_passes(total_passes, q_align, sms, cps,
                                   std::max(q_align, p_max - p_max % q_align), fine);
-  return fine < 0.97 * whole ? pf : pw;
+  return fine < 0.98 * whole ? pf : pw;
 }
 
 }  // namespace
