@@ -467,6 +467,16 @@ cudaError_t qg_decoder_step_at(qg_decoder dec, const float* x, uint32_t* pos_dev
                                cudaStream_t stream);
 /* Device pointers of the last step's final hidden state and this rank's logits. */
 cudaError_t qg_decoder_views(qg_decoder dec, float** hidden, float** logits);
+/* Device pointers of the last step's vectors of its last layer (no reference
+ * counterpart; for stage-by-stage checks and debugging): the layer's input (the residual
+ * stream, full width), this rank's Q/K/V rows before RoPE, its attention output, the
+ * residual after the attention block (full width), its gate / up / silu(gate)*up rows,
+ * the final hidden state and this rank's logits.  The workspace is reused by the next
+ * step.  cudaErrorNotReady before the first step. */
+typedef struct qg_decoder_stage_views {
+  float *layer_input, *q, *k, *v, *attn, *x1, *g, *u, *a, *hidden, *logits;
+} qg_decoder_stage_views;
+cudaError_t qg_decoder_stage_buffers(qg_decoder dec, qg_decoder_stage_views* views);
 cudaError_t qg_decoder_destroy(qg_decoder dec);
 
 /* ---------------------------------------------------------------------------

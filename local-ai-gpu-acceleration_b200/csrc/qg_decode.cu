@@ -175,6 +175,7 @@ struct qg_decoder_s {
   uint8_t* ws = nullptr;
   ncclComm_t comm = nullptr;
   uint32_t last_output = 0;  // workspace offset of the last step's final hidden state
+  const float* last_input = nullptr;  // the last step's input of its last layer
   uint8_t* ex_local = nullptr;                   // this rank's exchange region
   bool ex_owned = false;                         // allocated here (else caller-owned)
   uint8_t* ex_peer[qg::kMaxExchangeRanks] = {};  // every rank's region (self included)
@@ -494,6 +495,7 @@ cudaError_t decoder_step(qg_decoder dec, const float* x, uint32_t pos, uint32_t*
     const bool gathered = pending;
     QG_TRY(norm(cur, x_in, W.attn_norm));
     if (gathered) cur = x_in;
+    if (l + 1u == d.layers) dec->last_input = cur;
     {
       const uint8_t* p[3] = {W.wq, W.wk, W.wv};
       const uint8_t* m[3] = {W.wq_meta, W.wk_meta, W.wv_meta};
@@ -571,6 +573,25 @@ cudaError_t qg_decoder_views(qg_decoder dec, float** hidden_out, float** logits)
   if (dec == nullptr) return cudaErrorInvalidValue;
   if (hidden_out) *hidden_out = reinterpret_cast<float*>(dec->ws + dec->last_output);
   if (logits) *logits = reinterpret_cast<float*>(dec->ws + dec->lay.logits);
+  return cudaSuccess;
+}
+
+cudaError_t qg_decoder_stage_buffers(qg_decoder dec, qg_decoder_stage_views* v) {
+  if (dec == nullptr || v == nullptr) return cudaErrorInvalidValue;
+  if (dec->last_input == nullptr) return cudaErrorNotReady;  // no step enqueued yet
+  auto F = [&](size_t off) { return reinterpret_cast<float*>(dec->ws + off); };
+  const Layout& L = dec->lay;
+  v->layer_input = const_cast<float*>(dec->last_input);
+  v->q = F(L.q);
+  v->k = F(L.k);
+  v->v = F(L.v);
+  v->attn = F(L.attn);
+  v->x1 = F(L.x1);
+  v->g = F(L.g);
+  v->u = F(L.u);
+  v->a = F(L.a);
+  v->hidden = F(dec->last_output);
+  v->logits = F(L.logits);
   return cudaSuccess;
 }
 

@@ -88,6 +88,7 @@ SIGNATURES: dict[str, list] = {
     "qg_decoder_step": [P, P, U32, P, P],
     "qg_decoder_step_at": [P, P, P, U32, U32, P, P],
     "qg_decoder_views": [P, P, P],
+    "qg_decoder_stage_buffers": [P, P],
     "qg_decoder_destroy": [P],
     "qg_gguf_open": [ctypes.c_char_p, P],
     "qg_gguf_summary": [P, P],

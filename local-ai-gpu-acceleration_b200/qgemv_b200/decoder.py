@@ -298,6 +298,8 @@ class Decoder:
         fnorm = t(weights["final_norm"]).float().contiguous()
         self._keep.append(fnorm)
         head_p, head_m = pack_ptrs(weights["head"])
+        self.vocab_rows = (weights.get("shard") or {}).get("vocab_rows",
+                                                           getattr(weights["head"], "rows", None))
         self.dims = dims_struct(spec, rank, tp, collective)
         n = ctypes.c_size_t(0)
         check("qg_decoder_workspace_bytes", ctypes.byref(self.dims), ctypes.byref(n))
@@ -339,6 +341,32 @@ class Decoder:
         check("qg_decoder_views", self.handle, ctypes.byref(hp), ctypes.byref(lp))
         off = hp.value - self.workspace.data_ptr()
         return self.workspace[off: off + 4 * self.spec.hidden].view(torch.float32)
+
+    STAGES = ("layer_input", "q", "k", "v", "attn", "x1", "g", "u", "a", "hidden", "logits")
+
+    def stage_views(self) -> dict:
+        """The last step's vectors of its last layer (qg_decoder_stage_buffers) as float32
+        views of the workspace; the layer input is None when it is the caller's x (a
+        one-layer model)."""
+        raw = (c_void_p * len(self.STAGES))()
+        check("qg_decoder_stage_buffers", self.handle, ctypes.byref(raw))
+        s = self.spec
+        q_rows = s.n_q_heads // self.tp * s.head_dim
+        kv_rows = s.n_kv_heads // self.tp * s.head_dim
+        ffn = s.ffn // self.tp
+        sizes = dict(layer_input=s.hidden, q=q_rows, k=kv_rows, v=kv_rows, attn=q_rows,
+                     x1=s.hidden, g=ffn, u=ffn, a=ffn, hidden=s.hidden,
+                     logits=self.vocab_rows)
+        base, end = self.workspace.data_ptr(), self.workspace.data_ptr() + self.workspace.numel()
+        out = {}
+        for name, ptr in zip(self.STAGES, raw):
+            n = sizes[name]
+            if ptr is None or not (base <= ptr < end) or n is None:
+                out[name] = None
+                continue
+            off = ptr - base
+            out[name] = self.workspace[off: off + 4 * n].view(torch.float32)
+        return out
 
     def close(self) -> None:
         if self.handle.value:
