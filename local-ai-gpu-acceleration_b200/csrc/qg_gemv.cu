@@ -513,13 +513,15 @@ __global__ void __launch_bounds__(MAXT, 1) gemv_tiled_kernel(const GemvArgs a) {
           float v[4];
 #pragma unroll
           for (uint32_t r = 0; r < 4u; ++r) {
+            // Decoded unconditionally and selected, so the rows form one block the
+            // compiler can interleave: a row past the tile (or a thread past the pass)
+            // reads stale bytes of this stage -- inside the stage buffer, every codebook
+            // index in range -- and its value is dropped.
             const uint32_t lr = lr0 + (q + r) * a.rpp;
-            v[r] = 0.f;
-            if (valid && lr < nrows && !failed) {
-              const uint32_t ls = (q + r) * a.rpp + slot;
-              v[r] = chunk_dot<FMT>(st + ls * row_stride, st + a.meta_off + ls * meta_stride, c,
-                                    xr, tables);
-            }
+            const uint32_t ls = (q + r) * a.rpp + slot;
+            const float val = chunk_dot<FMT>(st + ls * row_stride, st + a.meta_off + ls * meta_stride,
+                                             c, xr, tables);
+            v[r] = (valid && lr < nrows && !failed) ? val : 0.f;
           }
           const float u = warp_sum4(v, lane, G);
           const uint32_t lr = lr0 + (q + ((lane & (G >> 2)) ? 2u : 0u) + ((lane & (G >> 1)) ? 1u : 0u)) * a.rpp;
@@ -530,13 +532,15 @@ __global__ void __launch_bounds__(MAXT, 1) gemv_tiled_kernel(const GemvArgs a) {
           float v[2];
 #pragma unroll
           for (uint32_t r = 0; r < 2u; ++r) {
+            // Decoded unconditionally and selected, so the rows form one block the
+            // compiler can interleave: a row past the tile (or a thread past the pass)
+            // reads stale bytes of this stage -- inside the stage buffer, every codebook
+            // index in range -- and its value is dropped.
             const uint32_t lr = lr0 + (q + r) * a.rpp;
-            v[r] = 0.f;
-            if (valid && lr < nrows && !failed) {
-              const uint32_t ls = (q + r) * a.rpp + slot;
-              v[r] = chunk_dot<FMT>(st + ls * row_stride, st + a.meta_off + ls * meta_stride, c,
-                                    xr, tables);
-            }
+            const uint32_t ls = (q + r) * a.rpp + slot;
+            const float val = chunk_dot<FMT>(st + ls * row_stride, st + a.meta_off + ls * meta_stride,
+                                             c, xr, tables);
+            v[r] = (valid && lr < nrows && !failed) ? val : 0.f;
           }
           const float u = warp_sum2(v, lane, G);
           const uint32_t lr = lr0 + (q + ((lane & (G >> 1)) ? 1u : 0u)) * a.rpp;
