@@ -524,6 +524,10 @@ cudaError_t qg_get_error(uint32_t* error_bits);
  * measurement code: grid CTAs, threads per CTA, rows per tile and pipeline stages. */
 cudaError_t qg_gemv_plan(int fmt, uint32_t rows, uint32_t cols, uint32_t* grid,
                          uint32_t* threads, uint32_t* rows_per_tile, uint32_t* stages);
+/* The same plan for a device of `sms` SMs, computed on the host without a device
+ * (capacity planning; sms 0 plans for one SM). */
+cudaError_t qg_gemv_plan_sms(int fmt, uint32_t rows, uint32_t cols, uint32_t sms, uint32_t* grid,
+                             uint32_t* threads, uint32_t* rows_per_tile, uint32_t* stages);
 
 #ifdef __cplusplus
 }

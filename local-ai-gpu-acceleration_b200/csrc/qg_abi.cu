@@ -309,10 +309,16 @@ cudaError_t qg_get_error(uint32_t* error_bits) {
 
 cudaError_t qg_gemv_plan(int fmt, uint32_t rows, uint32_t cols, uint32_t* grid, uint32_t* threads,
                          uint32_t* rows_per_tile, uint32_t* stages) {
+  return qg_gemv_plan_sms(fmt, rows, cols, static_cast<uint32_t>(qg::device_sm_count()), grid,
+                          threads, rows_per_tile, stages);
+}
+
+cudaError_t qg_gemv_plan_sms(int fmt, uint32_t rows, uint32_t cols, uint32_t sms, uint32_t* grid,
+                             uint32_t* threads, uint32_t* rows_per_tile, uint32_t* stages) {
   if (!valid_fmt(fmt) || rows == 0u || cols < 256u || (cols % 256u) != 0u) {
     return cudaErrorInvalidValue;
   }
-  const qg::GemvPlan p = qg::plan_gemv(fmt, rows, cols, qg::device_sm_count());
+  const qg::GemvPlan p = qg::plan_gemv(fmt, rows, cols, static_cast<int>(sms));
   if (grid) *grid = p.grid;
   if (threads) *threads = p.threads;
   if (rows_per_tile) *rows_per_tile = p.rows_per_tile;

@@ -62,6 +62,7 @@ SIGNATURES: dict[str, list] = {
     "qg_argmax_token": [P, U32, P, U32, U32, U32, P],
     "qg_get_error": [P],
     "qg_gemv_plan": [c_int, U32, U32, P, P, P, P],
+    "qg_gemv_plan_sms": [c_int, U32, U32, U32, P, P, P, P],
     "qg_layer_slice_workspace_bytes": [P, P],
     "qg_layer_slice_buffers": [P, P, P],
     "qg_gemm_batched_workspace_bytes": [c_int, U32, U32, U32, P],

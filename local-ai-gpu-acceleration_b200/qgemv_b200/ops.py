@@ -126,6 +126,21 @@ def argmax_token(values: torch.Tensor, token: torch.Tensor, token_offset: int, a
           modulus, _stream(stream))
 
 
+def gemv_plan(fmt: int, rows: int, cols: int, sms: int | None = None) -> dict:
+    """The tiled GEMV's launch plan for a shape (qg_gemv_plan): on the current device, or,
+    with `sms`, for a device of that many SMs (host-side, no device needed)."""
+    import ctypes
+
+    vals = [ctypes.c_uint32(0) for _ in range(4)]
+    refs = [ctypes.addressof(v) for v in vals]
+    if sms is None:
+        check("qg_gemv_plan", fmt, rows, cols, *refs)
+    else:
+        check("qg_gemv_plan_sms", fmt, rows, cols, sms, *refs)
+    grid, threads, rows_per_tile, stages = (v.value for v in vals)
+    return dict(grid=grid, threads=threads, rows_per_tile=rows_per_tile, stages=stages)
+
+
 def get_error() -> int:
     import ctypes
 
