@@ -1,4 +1,4 @@
-"""Tensor-parallel sharding arithmetic on CPU ranks (gloo, world size 2 and 4): each rank runs
+"""Tensor-parallel sharding arithmetic on CPU ranks (gloo, world size 2, 4 and 8): each rank runs
 the oracle decode step on its own shards (row shards of Wq/Wk/Wv/Wg/Wu/head, column
 shards of Wo/Wd, its kv heads), with the residual on rank 0 and real gloo all-reduce /
 all-gather, and must reproduce the single-rank step."""
@@ -16,6 +16,9 @@ SPEC_KW = dict(layers=2, hidden=512, n_q_heads=4, n_kv_heads=2, head_dim=128, ff
                vocab=1000, ctx_max=64)
 # shards four ways: every rank 2 q heads, 1 kv head, 512 ffn rows, 256 vocab rows
 SPEC_KW_TP4 = dict(layers=2, hidden=1024, n_q_heads=8, n_kv_heads=4, head_dim=128, ffn=2048,
+                   vocab=1024, ctx_max=64)
+# eight ways: every rank 2 q heads, 1 kv head, 256 ffn rows, 128 vocab rows
+SPEC_KW_TP8 = dict(layers=2, hidden=1024, n_q_heads=16, n_kv_heads=8, head_dim=128, ffn=2048,
                    vocab=1024, ctx_max=64)
 POS = 37
 
@@ -55,7 +58,8 @@ def _rank_main(rank, world, port_no, q, spec_kw):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,spec_kw", [(2, SPEC_KW), (4, SPEC_KW_TP4)], ids=["tp2", "tp4"])
+@pytest.mark.parametrize("world,spec_kw", [(2, SPEC_KW), (4, SPEC_KW_TP4), (8, SPEC_KW_TP8)],
+                         ids=["tp2", "tp4", "tp8"])
 def test_tp_sharding_matches_single_rank(port, world, spec_kw):
     sys.path.insert(0, str(REPO / "oracle"))
     import decode_oracle
