@@ -897,7 +897,8 @@ uint32_t balanced_passes(uint32_t total_passes, uint32_t q, uint32_t q_align, ui
 
 // Plan of the tiled kernel.  Stage = Q passes of ~16 KB whose byte count is a multiple
 // of 16 (IQ formats: at least four passes); S stages within ~96 KB (2..8); tiles of P
-// passes (Q | P) balanced over the SMs (balanced_passes).
+// passes balanced over the SMs (balanced_passes: whole stages, or ending inside one when
+// that balances better).
 GemvPlan plan_gemv(int fmt, uint32_t rows, uint32_t cols, int sms, uint32_t group_cap) {
   GemvPlan p{};
   sms = std::max(sms, 1);  // no device (host-side plan query): plan for one SM
